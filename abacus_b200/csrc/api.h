@@ -1,0 +1,39 @@
+// Declarations of every op exported by the abacus_b200._C extension.
+#pragma once
+#include <torch/extension.h>
+#include <vector>
+
+namespace abacus {
+namespace gemm {
+void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
+              int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate, int64_t passes);
+void gemm_swiglu(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
+                 torch::Tensor h, int64_t passes);
+void gemm_swiglu_bwd(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u, torch::Tensor dgu,
+                     int64_t passes);
+}  // namespace gemm
+}  // namespace abacus
+
+namespace abacus {
+namespace ops {
+void rmsnorm_fwd(torch::Tensor x, torch::Tensor gamma, torch::Tensor y, torch::Tensor rstd, double eps);
+void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor gamma, torch::Tensor rstd, torch::Tensor dx,
+                 torch::Tensor dgamma);
+void qk_prologue_fwd(torch::Tensor qkv, torch::Tensor gq, torch::Tensor gk, torch::Tensor cos_t, torch::Tensor sin_t,
+                     c10::optional<torch::Tensor> positions, int64_t seq_len, torch::Tensor q_out, torch::Tensor k_out,
+                     torch::Tensor rstd, int64_t heads, int64_t head_dim, double eps);
+void qk_prologue_bwd(torch::Tensor qkv, torch::Tensor gq, torch::Tensor gk, torch::Tensor cos_t, torch::Tensor sin_t,
+                     c10::optional<torch::Tensor> positions, int64_t seq_len, torch::Tensor dq, torch::Tensor dk,
+                     torch::Tensor rstd, torch::Tensor dqkv, torch::Tensor dgq, torch::Tensor dgk, int64_t heads,
+                     int64_t head_dim);
+void embedding_fwd(torch::Tensor tokens, torch::Tensor weight, torch::Tensor out);
+void embedding_bwd(torch::Tensor sorted_tokens, torch::Tensor perm, torch::Tensor dy, torch::Tensor dw);
+void cross_entropy_fwd_bwd(torch::Tensor logits, torch::Tensor target, torch::Tensor loss, c10::optional<torch::Tensor> lse,
+                           int64_t ignore_index, torch::Tensor grad_scale, bool write_grad);
+void cross_entropy_grad(torch::Tensor logits, torch::Tensor grad, torch::Tensor target, torch::Tensor lse,
+                        int64_t ignore_index, torch::Tensor grad_scale);
+void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> grads, std::vector<torch::Tensor> exp_avgs,
+                std::vector<torch::Tensor> exp_avg_sqs, double lr, double beta1, double beta2, double eps,
+                double weight_decay, int64_t step);
+}  // namespace ops
+}  // namespace abacus

@@ -1,0 +1,21 @@
+// Python bindings of the abacus_b200._C extension (sm_100a kernels).
+#include <torch/extension.h>
+#include "api.h"
+#include "common/host.h"
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("gemm_out", &abacus::gemm::gemm_out, "tcgen05 tf32 / 3xTF32 GEMM into C");
+  m.def("gemm_swiglu", &abacus::gemm::gemm_swiglu, "gate/up GEMM with SwiGLU epilogue");
+  m.def("gemm_swiglu_bwd", &abacus::gemm::gemm_swiglu_bwd, "down-projection dgrad with SwiGLU backward epilogue");
+  m.def("rmsnorm_fwd", &abacus::ops::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &abacus::ops::rmsnorm_bwd);
+  m.def("qk_prologue_fwd", &abacus::ops::qk_prologue_fwd);
+  m.def("qk_prologue_bwd", &abacus::ops::qk_prologue_bwd);
+  m.def("embedding_fwd", &abacus::ops::embedding_fwd);
+  m.def("embedding_bwd", &abacus::ops::embedding_bwd);
+  m.def("cross_entropy_fwd_bwd", &abacus::ops::cross_entropy_fwd_bwd);
+  m.def("cross_entropy_grad", &abacus::ops::cross_entropy_grad);
+  m.def("adamw_step", &abacus::ops::adamw_step);
+  m.def("read_status", &abacus::host::read_status, "device status word (0 = healthy)");
+  m.def("reset_status", &abacus::host::reset_status, "clear the device status word");
+}

@@ -1,0 +1,216 @@
+// Host side of the tcgen05 tf32 GEMM: tensor-map encoding, tile-config
+// selection and the torch bindings used by abacus_b200.ops.linear.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+#include "gemm_launch.cuh"
+#include "../common/host.h"
+#include "../api.h"
+
+namespace abacus {
+namespace gemm {
+
+namespace {
+
+// 2-D fp32 tensor map over a row-major matrix with `rows` rows of `inner`
+// elements and a row stride of `ld` elements; box = box_inner x box_rows.
+CUtensorMap make_map(const float* base, int64_t inner, int64_t rows, int64_t ld, int box_inner, int box_rows,
+                     bool mn_major) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 4)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  CUresult r = host::encode_tiled()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+                                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", static_cast<int>(r), " (inner=", inner,
+              " rows=", rows, " ld=", ld, ")");
+  return m;
+}
+
+// Operand view: logical (rows_mn, k) matrix stored either K-major
+// (row-major [mn][k]) or MN-major (row-major [k][mn]).
+struct Operand {
+  const float* ptr;
+  int64_t mn, k, ld;
+  bool mn_major;
+};
+
+Operand operand_of(const torch::Tensor& t, bool transposed_storage, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32, name, " must be a CUDA fp32 tensor");
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must have unit inner stride");
+  TORCH_CHECK(t.stride(0) % 4 == 0 && t.stride(0) >= t.size(1), name,
+              " row stride must be a multiple of 4 elements (16 bytes) for TMA");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned for TMA");
+  Operand o;
+  o.ptr = t.data_ptr<float>();
+  o.ld = t.stride(0);
+  o.mn_major = transposed_storage;
+  if (transposed_storage) {  // stored [k][mn]
+    o.k = t.size(0);
+    o.mn = t.size(1);
+  } else {  // stored [mn][k]
+    o.mn = t.size(0);
+    o.k = t.size(1);
+  }
+  return o;
+}
+
+CUtensorMap map_for(const Operand& o, int tile_mn) {
+  if (o.mn_major) return make_map(o.ptr, o.mn, o.k, o.ld, 32, BK, true);
+  return make_map(o.ptr, o.k, o.mn, o.ld, BK, tile_mn, false);
+}
+
+void check_passes(int64_t passes) { TORCH_CHECK(passes == 1 || passes == 3, "passes must be 1 (tf32) or 3 (3xTF32)"); }
+
+}  // namespace
+
+// C = alpha * op(A) @ op(B) [+ residual] [+ C]
+//   a: (M, K), or (K, M) when trans_a
+//   b list: each (K, N_i) row-major, or (N_i, K) when trans_b
+//   b_mode: 0 single, 1 segmented along N (C columns = concat of B_i),
+//           2 segmented along K (A columns = concat of K_i)
+void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
+              int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate, int64_t passes) {
+  check_passes(passes);
+  TORCH_CHECK(!bs.empty() && bs.size() <= 3, "between 1 and 3 B operands");
+  const c10::cuda::CUDAGuard guard(a.device());
+  Operand A = operand_of(a, trans_a, "A");
+  std::vector<Operand> B;
+  for (auto& b : bs) B.push_back(operand_of(b, !trans_b, "B"));
+  int64_t M = A.mn, K = A.k, N = 0, seg = 0;
+  if (b_mode == kBSingle) {
+    TORCH_CHECK(bs.size() == 1);
+    N = B[0].mn;
+    TORCH_CHECK(B[0].k == K, "inner dimensions differ: ", K, " vs ", B[0].k);
+  } else if (b_mode == kBSegN) {
+    seg = B[0].mn;
+    for (auto& o : B) TORCH_CHECK(o.mn == seg && o.k == K, "segmented-N operands must share shape");
+    N = seg * static_cast<int64_t>(B.size());
+  } else if (b_mode == kBSegK) {
+    seg = B[0].k;
+    N = B[0].mn;
+    for (auto& o : B) TORCH_CHECK(o.k == seg && o.mn == N, "segmented-K operands must share shape");
+    TORCH_CHECK(K == seg * static_cast<int64_t>(B.size()), "A width must equal the sum of the K segments");
+  } else {
+    TORCH_CHECK(false, "bad b_mode");
+  }
+  TORCH_CHECK(c.is_cuda() && c.scalar_type() == torch::kFloat32 && c.dim() == 2 && c.stride(1) == 1, "bad C");
+  TORCH_CHECK(c.size(0) == M && c.size(1) == N, "C shape mismatch");
+  TORCH_CHECK(c.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0, "C must be 16-byte aligned rows");
+  if (M == 0 || N == 0) return;
+  if (K == 0) {
+    if (!accumulate) c.zero_();
+    if (residual) c.add_(*residual);
+    return;
+  }
+  int BN = pick_bn(N, static_cast<int>(passes));
+  if (b_mode == kBSegN && seg % BN != 0) BN = 128;
+  if (b_mode == kBSegN) TORCH_CHECK(seg % BN == 0, "segment width ", seg, " must be a multiple of the N tile ", BN);
+  if (b_mode == kBSegK) TORCH_CHECK(seg % BK == 0, "segment depth must be a multiple of ", BK);
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.tma_a = map_for(A, BM);
+  for (size_t i = 0; i < B.size(); ++i) p.tma_b[i] = map_for(B[i], BN);
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.b_mode = static_cast<int>(b_mode);
+  p.seg = static_cast<int>(seg);
+  p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
+  p.alpha = static_cast<float>(alpha);
+  p.c = c.data_ptr<float>();
+  p.ldc = c.stride(0);
+  if (residual) {
+    TORCH_CHECK(residual->sizes() == c.sizes() && residual->stride(1) == 1 && residual->stride(0) % 4 == 0, "bad residual");
+    p.r = residual->data_ptr<float>();
+    p.ldr = residual->stride(0);
+  }
+  p.accumulate = accumulate ? 1 : 0;
+  p.status = host::status_ptr(a.device().index());
+  const int grid = static_cast<int>(((M + BM - 1) / BM) * p.num_n_tiles);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_store(p, grid, BN, A.mn_major, B[0].mn_major, static_cast<int>(passes), stream);
+}
+
+// SwiGLU up-projection: g = x @ w_gate, u = x @ w_up, h = silu(g) * u.
+// x (T, D), w_gate / w_up (D, Mh) in the (in, out) layout.
+void gemm_swiglu(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
+                 torch::Tensor h, int64_t passes) {
+  check_passes(passes);
+  const c10::cuda::CUDAGuard guard(x.device());
+  Operand A = operand_of(x, false, "x");
+  Operand Bg = operand_of(w_gate, true, "w_gate");
+  Operand Bu = operand_of(w_up, true, "w_up");
+  TORCH_CHECK(Bg.k == A.k && Bu.k == A.k && Bg.mn == Bu.mn, "SwiGLU shapes");
+  const int64_t T = A.mn, Mh = Bg.mn;
+  for (auto* t : {&g, &u, &h}) {
+    TORCH_CHECK(t->size(0) == T && t->size(1) == Mh && t->stride(1) == 1 && t->stride(0) == h.stride(0),
+                "SwiGLU outputs must be (T, hidden) with a shared row stride");
+  }
+  if (T == 0 || Mh == 0) return;
+  const int BN = passes == 3 ? 128 : 256;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.tma_a = map_for(A, BM);
+  p.tma_b[0] = map_for(Bg, BN / 2);
+  p.tma_b[1] = map_for(Bu, BN / 2);
+  p.M = static_cast<int>(T);
+  p.N = static_cast<int>(Mh);
+  p.K = static_cast<int>(A.k);
+  p.b_mode = kBDualN;
+  p.num_n_tiles = static_cast<int>((Mh + BN / 2 - 1) / (BN / 2));
+  p.alpha = 1.f;
+  p.g = g.data_ptr<float>();
+  p.u = u.data_ptr<float>();
+  p.h = h.data_ptr<float>();
+  p.ldh = h.stride(0);
+  p.status = host::status_ptr(x.device().index());
+  const int grid = static_cast<int>(((T + BM - 1) / BM) * p.num_n_tiles);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_swiglu(p, grid, BN, static_cast<int>(passes), stream);
+}
+
+// SwiGLU backward through the hidden layer: dh = dy @ w_down^T, then
+// dgu[:, :Mh] = dh * u * silu'(g), dgu[:, Mh:] = dh * silu(g).
+void gemm_swiglu_bwd(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u, torch::Tensor dgu,
+                     int64_t passes) {
+  check_passes(passes);
+  const c10::cuda::CUDAGuard guard(dy.device());
+  Operand A = operand_of(dy, false, "dy");
+  // w_down is (Mh, D): as B (K = D, N = Mh) it is stored [N][K], i.e. K-major.
+  Operand B = operand_of(w_down, false, "w_down");
+  TORCH_CHECK(B.k == A.k, "w_down shape");
+  const int64_t T = A.mn, Mh = B.mn;
+  TORCH_CHECK(g.size(0) == T && g.size(1) == Mh && u.sizes() == g.sizes() && u.stride(0) == g.stride(0), "g/u shape");
+  TORCH_CHECK(dgu.size(0) == T && dgu.size(1) == 2 * Mh, "dgu must be (T, 2*hidden)");
+  if (T == 0 || Mh == 0) return;
+  const int BN = passes == 3 ? 128 : (Mh >= 2048 ? 256 : 128);
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.tma_a = map_for(A, BM);
+  p.tma_b[0] = map_for(B, BN);
+  p.M = static_cast<int>(T);
+  p.N = static_cast<int>(Mh);
+  p.K = static_cast<int>(A.k);
+  p.b_mode = kBSingle;
+  p.num_n_tiles = static_cast<int>((Mh + BN - 1) / BN);
+  p.alpha = 1.f;
+  p.g_in = g.data_ptr<float>();
+  p.u_in = u.data_ptr<float>();
+  p.ld_gu = g.stride(0);
+  p.dgu = dgu.data_ptr<float>();
+  p.ld_dgu = dgu.stride(0);
+  p.status = host::status_ptr(dy.device().index());
+  const int grid = static_cast<int>(((T + BM - 1) / BM) * p.num_n_tiles);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_swiglu_bwd(p, grid, BN, static_cast<int>(passes), stream);
+}
+
+}  // namespace gemm
+}  // namespace abacus
+

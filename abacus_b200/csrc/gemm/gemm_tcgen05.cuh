@@ -1,0 +1,422 @@
+// tcgen05 (kind::tf32) GEMM for sm_100a: C[M,N] = A[M,K] * B[K,N] in fp32
+// storage with an fp32 TMEM accumulator.
+//
+// * One CTA computes one 128 x BN output tile.
+// * Warp 0: TMA producer. Warp 1: TMEM allocator + single-thread MMA issuer.
+//   Warps 2-5: epilogue (TMEM -> registers -> global). Warps 6-9 (3xTF32
+//   only): split-precision converter that rewrites each landed stage as
+//   hi = tf32(x) in place and lo = tf32(x - hi) beside it, so the MMA warp
+//   can issue lo*hi + hi*lo + hi*hi (fp32-level accuracy on tensor cores).
+// * Operands may be K-major (row-major along K; TMA SWIZZLE_128B) or MN-major
+//   (row-major along M/N; TMA SWIZZLE_128B_ATOM_32B, the only MN-major layout
+//   tcgen05 accepts for 32-bit operands). So x@W, dY@W^T and X^T@dY all run
+//   without a transpose copy.
+// * B may come from up to three tensors: segmented along N (fused QKV),
+//   segmented along K (dX of fused QKV / SwiGLU), or paired along N (the
+//   gate|up halves of a SwiGLU tile).
+// * Epilogues: store (alpha, residual, accumulate), SwiGLU forward (writes
+//   gate, up and silu(gate)*up), SwiGLU backward (dgate, dup from dh).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "../common/sm100.cuh"
+
+namespace abacus {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 32;  // fp32 elements = 128 bytes, one swizzle span
+
+enum BMode : int { kBSingle = 0, kBSegN = 1, kBSegK = 2, kBDualN = 3 };
+enum Epi : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiSwiGLUBwd = 2 };
+
+struct alignas(64) Params {
+  CUtensorMap tma_a;
+  CUtensorMap tma_b[3];
+  int M, N, K;       // N is the logical output width (hidden units for SwiGLU)
+  int b_mode;
+  int seg;           // segment length (elements) for kBSegN / kBSegK
+  int num_n_tiles;
+  float alpha;
+  float* c;
+  long long ldc;
+  const float* r;    // residual added by the store epilogue (nullable)
+  long long ldr;
+  int accumulate;    // store epilogue: C += result
+  // SwiGLU forward outputs (ld = ldh)
+  float* g;
+  float* u;
+  float* h;
+  long long ldh;
+  // SwiGLU backward: inputs gate/up (ld = ld_gu) and output [dgate | dup] rows
+  const float* g_in;
+  const float* u_in;
+  long long ld_gu;
+  float* dgu;
+  long long ld_dgu;
+  int* status;
+};
+
+template <int BN, bool A_MN, bool B_MN, int PASSES, int STAGES>
+struct Config {
+  static constexpr int kABytes = BM * BK * 4;
+  static constexpr int kBBytes = BN * BK * 4;
+  static constexpr int kStageBytes = (kABytes + kBBytes) * (PASSES == 3 ? 2 : 1);
+  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024;
+  static constexpr int kThreads = PASSES == 3 ? 320 : 192;
+  // 3xTF32 accumulates K in chunks of kChunk k-tiles into two alternating
+  // TMEM buffers that the epilogue drains (see the epilogue).
+  static constexpr bool kChunked = PASSES == 3;
+  static constexpr int kChunk = 2;
+  static constexpr int kAccCols = kChunked ? 2 * BN : BN;
+  static constexpr uint32_t kTmemCols = kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
+};
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int BN, bool A_MN, bool B_MN, int PASSES, int EPI, int STAGES>
+__global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThreads, 1)
+    gemm_kernel(const __grid_constant__ Params p) {
+  using Cfg = Config<BN, A_MN, B_MN, PASSES, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full_bar[STAGES];
+  __shared__ uint64_t empty_bar[STAGES];
+  __shared__ uint64_t conv_bar[STAGES];
+  __shared__ uint64_t accum_bar;
+  __shared__ uint64_t chunk_full[2];
+  __shared__ uint64_t chunk_empty[2];
+  __shared__ uint32_t tmem_base_slot;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (*reinterpret_cast<volatile int*>(p.status) != kStatusOk) return;
+
+  // 1024-byte aligned stage buffers (swizzle period of SWIZZLE_128B).
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  auto stage_a = [&](int s) { return smem + s * Cfg::kStageBytes; };
+  auto stage_b = [&](int s) { return smem + s * Cfg::kStageBytes + Cfg::kABytes; };
+  auto stage_alo = [&](int s) { return smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes; };
+  auto stage_blo = [&](int s) { return smem + s * Cfg::kStageBytes + 2 * Cfg::kABytes + Cfg::kBBytes; };
+
+  // Tile coordinates, grouped along M for L2 reuse of B.
+  const int num_m_tiles = (p.M + BM - 1) / BM;
+  const int num_n_tiles = p.num_n_tiles;
+  constexpr int kGroup = 16;
+  const int tile = blockIdx.x;
+  const int group = tile / (kGroup * num_n_tiles);
+  const int first_m = group * kGroup;
+  const int group_m = min(num_m_tiles - first_m, kGroup);
+  const int in_group = tile - group * kGroup * num_n_tiles;
+  const int m_tile = first_m + in_group % group_m;
+  const int n_tile = in_group / group_m;
+  const int m0 = m_tile * BM;
+  // Output column base. For SwiGLU forward a tile covers BN/2 hidden units.
+  const int n0 = n_tile * (EPI == kEpiSwiGLU ? BN / 2 : BN);
+  const int num_k = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+      mbar_init(&conv_bar[s], 128);
+    }
+    mbar_init(&accum_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&chunk_full[b], 1);
+      mbar_init(&chunk_empty[b], 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tma_a);
+    tma_prefetch_desc(&p.tma_b[0]);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_sync()) {
+      int issued = 0;
+      for (int kt = 0; kt < num_k; ++kt) {
+        const int s = kt % STAGES;
+        const int use = kt / STAGES;
+        if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+        const int k0 = kt * BK;
+        mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
+        if (A_MN) {
+#pragma unroll
+          for (int c = 0; c < BM / 32; ++c) tma_load_2d(stage_a(s) + c * 32 * BK * 4, &p.tma_a, &full_bar[s], m0 + 32 * c, k0);
+        } else {
+          tma_load_2d(stage_a(s), &p.tma_a, &full_bar[s], k0, m0);
+        }
+        // B source for this (n, k) tile.
+        const CUtensorMap* bmap = &p.tma_b[0];
+        int bn = n0, bk = k0;
+        if (p.b_mode == kBSegN) {
+          const int sidx = n0 / p.seg;
+          bmap = &p.tma_b[sidx];
+          bn = n0 - sidx * p.seg;
+        } else if (p.b_mode == kBSegK) {
+          const int sidx = k0 / p.seg;
+          bmap = &p.tma_b[sidx];
+          bk = k0 - sidx * p.seg;
+        }
+        if (B_MN) {
+          if (p.b_mode == kBDualN) {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) {
+              tma_load_2d(stage_b(s) + c * 32 * BK * 4, &p.tma_b[0], &full_bar[s], n0 + 32 * c, k0);
+              tma_load_2d(stage_b(s) + (c + BN / 64) * 32 * BK * 4, &p.tma_b[1], &full_bar[s], n0 + 32 * c, k0);
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) tma_load_2d(stage_b(s) + c * 32 * BK * 4, bmap, &full_bar[s], bn + 32 * c, bk);
+          }
+        } else {
+          if (p.b_mode == kBDualN) {
+            tma_load_2d(stage_b(s), &p.tma_b[0], &full_bar[s], k0, n0);
+            tma_load_2d(stage_b(s) + (BN / 2) * BK * 4, &p.tma_b[1], &full_bar[s], k0, n0);
+          } else {
+            tma_load_2d(stage_b(s), bmap, &full_bar[s], bk, bn);
+          }
+        }
+        ++issued;
+      }
+      // Never leave a bulk copy in flight into a CTA that is about to exit.
+      for (int kt = max(0, issued - STAGES); kt < issued; ++kt) {
+        mbar_wait(&full_bar[kt % STAGES], (kt / STAGES) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
+      bool issued_any = false;
+      for (int kt = 0; kt < num_k; ++kt) {
+        const int s = kt % STAGES;
+        const int use = kt / STAGES;
+        const int chunk = kt / Cfg::kChunk;
+        const int buf = Cfg::kChunked ? (chunk & 1) : 0;
+        const bool first_in_chunk = Cfg::kChunked ? (kt % Cfg::kChunk == 0) : (kt == 0);
+        const bool last_in_chunk = Cfg::kChunked && (kt % Cfg::kChunk == Cfg::kChunk - 1 || kt == num_k - 1);
+        if (Cfg::kChunked && first_in_chunk && chunk >= 2 &&
+            !mbar_wait(&chunk_empty[buf], ((chunk >> 1) - 1) & 1, p.status, kStatusTimeoutAccum))
+          break;
+        uint64_t* ready = PASSES == 3 ? &conv_bar[s] : &full_bar[s];
+        if (!mbar_wait(ready, use & 1, p.status, PASSES == 3 ? kStatusTimeoutConvert : kStatusTimeoutFull)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+        const uint32_t a_hi = smem_u32(stage_a(s));
+        const uint32_t b_hi = smem_u32(stage_b(s));
+#pragma unroll
+        for (int ks = 0; ks < BK / 8; ++ks) {
+          // One MMA consumes K = 8 tf32 elements (32 bytes).
+          const uint32_t a_off = A_MN ? ks * 8 * 128 : ks * 32;
+          const uint32_t b_off = B_MN ? ks * 8 * 128 : ks * 32;
+          auto desc_a = [&](uint32_t base) {
+            return A_MN ? desc_mnmajor_sw128_32b(base + a_off, 32 * BK * 4) : desc_kmajor_sw128(base + a_off);
+          };
+          auto desc_b = [&](uint32_t base) {
+            return B_MN ? desc_mnmajor_sw128_32b(base + b_off, 32 * BK * 4) : desc_kmajor_sw128(base + b_off);
+          };
+          const uint32_t acc = (first_in_chunk && ks == 0) ? 0u : 1u;
+          if (PASSES == 3) {
+            const uint32_t a_lo = smem_u32(stage_alo(s));
+            const uint32_t b_lo = smem_u32(stage_blo(s));
+            mma_tf32_ss(d_tmem, desc_a(a_lo), desc_b(b_hi), idesc, acc);
+            mma_tf32_ss(d_tmem, desc_a(a_hi), desc_b(b_lo), idesc, 1u);
+            mma_tf32_ss(d_tmem, desc_a(a_hi), desc_b(b_hi), idesc, 1u);
+          } else {
+            mma_tf32_ss(d_tmem, desc_a(a_hi), desc_b(b_hi), idesc, acc);
+          }
+        }
+        mma_commit(&empty_bar[s]);
+        if (last_in_chunk) mma_commit(&chunk_full[buf]);
+        issued_any = true;
+      }
+      if (!Cfg::kChunked) {
+        if (issued_any) mma_commit(&accum_bar);
+        else if (num_k == 0) mbar_arrive(&accum_bar);
+      }
+      // Every commit must have landed before this CTA's shared memory is
+      // released: wait for the last release of each stage (bounded).
+      for (int kt = max(0, num_k - STAGES); kt < num_k && issued_any; ++kt) {
+        if (!mbar_wait(&empty_bar[kt % STAGES], (kt / STAGES) & 1, p.status, kStatusTimeoutEmpty)) break;
+      }
+    }
+  } else if (warp >= 2 && warp < 6) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp % 4;  // TMEM lane quarter this warp may access
+    const int row = m0 + q * 32 + lane;
+    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    bool ok = num_k > 0;
+    // fp32 (3xTF32) mode: drain each K-chunk accumulator into registers with
+    // round-to-nearest fp32 adds, so the tensor core's own accumulation never
+    // spans more than kChunk k-tiles.
+    float acc[Cfg::kChunked ? BN : 1];
+    if constexpr (Cfg::kChunked) {
+#pragma unroll
+      for (int i = 0; i < BN; ++i) acc[i] = 0.f;
+      const int num_chunks = (num_k + Cfg::kChunk - 1) / Cfg::kChunk;
+      for (int j = 0; j < num_chunks && ok; ++j) {
+        const int buf = j & 1;
+        if (!mbar_wait(&chunk_full[buf], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(taddr + buf * BN + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c * 32 + i] += __uint_as_float(v[i]);
+        }
+        tc_fence_before();
+        mbar_arrive(&chunk_empty[buf]);
+      }
+    } else {
+      ok = ok && mbar_wait(&accum_bar, 0, p.status, kStatusTimeoutAccum);
+      tc_fence_after();
+    }
+    // Fetch the 32 accumulator columns of group c.
+    auto group = [&](int c, float (&out)[32]) {
+      if constexpr (Cfg::kChunked) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) out[i] = acc[c * 32 + i];
+      } else {
+        uint32_t v[32];
+        tmem_ld32(taddr + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) out[i] = __uint_as_float(v[i]);
+      }
+    };
+    const bool row_ok = row < p.M;
+    if (ok && EPI == kEpiStore) {
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        group(c, v);
+        const int col0 = n0 + c * 32;
+        if (row_ok && col0 < p.N) {
+          float* crow = p.c + static_cast<long long>(row) * p.ldc + col0;
+          const float* rrow = p.r ? p.r + static_cast<long long>(row) * p.ldr + col0 : nullptr;
+          if (col0 + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 o = make_float4(v[j] * p.alpha, v[j + 1] * p.alpha, v[j + 2] * p.alpha, v[j + 3] * p.alpha);
+              if (rrow) {
+                const float4 rv = *reinterpret_cast<const float4*>(rrow + j);
+                o.x += rv.x; o.y += rv.y; o.z += rv.z; o.w += rv.w;
+              }
+              if (p.accumulate) {
+                const float4 cv = *reinterpret_cast<const float4*>(crow + j);
+                o.x += cv.x; o.y += cv.y; o.z += cv.z; o.w += cv.w;
+              }
+              *reinterpret_cast<float4*>(crow + j) = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (col0 + j < p.N) {
+                float o = v[j] * p.alpha;
+                if (rrow) o += rrow[j];
+                if (p.accumulate) o += crow[j];
+                crow[j] = o;
+              }
+            }
+          }
+        }
+      }
+    } else if (ok && EPI == kEpiSwiGLU) {
+#pragma unroll
+      for (int c = 0; c < BN / 64; ++c) {
+        float gv[32], uv[32];
+        group(c, gv);
+        group(c + BN / 64, uv);
+        const int col0 = n0 + c * 32;
+        if (row_ok && col0 < p.N) {
+          const long long off = static_cast<long long>(row) * p.ldh + col0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j < p.N) {
+              p.g[off + j] = gv[j];
+              p.u[off + j] = uv[j];
+              p.h[off + j] = silu_f(gv[j]) * uv[j];
+            }
+          }
+        }
+      }
+    } else if (ok && EPI == kEpiSwiGLUBwd) {
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        group(c, v);
+        const int col0 = n0 + c * 32;
+        if (row_ok && col0 < p.N) {
+          const long long off = static_cast<long long>(row) * p.ld_gu + col0;
+          const long long doff = static_cast<long long>(row) * p.ld_dgu + col0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j < p.N) {
+              const float dh = v[j];
+              const float g = p.g_in[off + j];
+              const float u = p.u_in[off + j];
+              const float sg = 1.0f / (1.0f + __expf(-g));
+              p.dgu[doff + j] = dh * u * sg * (1.0f + g * (1.0f - sg));
+              p.dgu[doff + p.N + j] = dh * g * sg;
+            }
+          }
+        }
+      }
+    }
+  } else if (PASSES == 3 && warp >= 6) {
+    // ------------------------------------------------------------ converter
+    const int ct = threadIdx.x - 192;  // 0..127
+    for (int kt = 0; kt < num_k; ++kt) {
+      const int s = kt % STAGES;
+      const int use = kt / STAGES;
+      if (!mbar_wait(&full_bar[s], use & 1, p.status, kStatusTimeoutFull)) break;
+      // A and B hi/lo regions are each contiguous; swizzling only permutes
+      // positions, so an elementwise pass over the bytes is layout-agnostic.
+      float4* a = reinterpret_cast<float4*>(stage_a(s));
+      float4* alo = reinterpret_cast<float4*>(stage_alo(s));
+      constexpr int kA4 = BM * BK / 4;
+      constexpr int kB4 = BN * BK / 4;
+#pragma unroll 4
+      for (int i = ct; i < kA4 + kB4; i += 128) {
+        float4* src = i < kA4 ? a + i : reinterpret_cast<float4*>(stage_b(s)) + (i - kA4);
+        float4* dst = i < kA4 ? alo + i : reinterpret_cast<float4*>(stage_blo(s)) + (i - kA4);
+        float4 x = *src;
+        float4 hi = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
+        float4 lo = make_float4(to_tf32(x.x - hi.x), to_tf32(x.y - hi.y), to_tf32(x.z - hi.z), to_tf32(x.w - hi.w));
+        *src = hi;
+        *dst = lo;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&conv_bar[s]);
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace gemm
+}  // namespace abacus

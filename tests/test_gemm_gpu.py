@@ -1,0 +1,122 @@
+"""tcgen05 GEMM numerics against an fp64 PyTorch reference of the same op."""
+import itertools
+
+import pytest
+import torch
+
+from abacus_b200.ops import gemm, precision
+from abacus_b200.ops._ext import check_status
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(a, b, trans_a, trans_b):
+    lhs = a.double().t() if trans_a else a.double()
+    rhs = b.double().t() if trans_b else b.double()
+    return lhs @ rhs
+
+
+def _rel_err(out, ref):
+    return ((out.double() - ref).abs().max() / ref.abs().max()).item()
+
+
+SHAPES = [(128, 128, 32), (256, 256, 64), (200, 136, 72), (384, 512, 768), (1000, 2304, 768), (130, 300, 1028)]
+
+
+@pytest.mark.parametrize("mode", ["tf32", "fp32"])
+@pytest.mark.parametrize("trans_a,trans_b", list(itertools.product([False, True], repeat=2)))
+@pytest.mark.parametrize("shape", SHAPES)
+def test_gemm_layouts(mode, trans_a, trans_b, shape):
+    m, n, k = shape
+    torch.manual_seed(0)
+    a = torch.randn(k, m, device="cuda") if trans_a else torch.randn(m, k, device="cuda")
+    b = torch.randn(n, k, device="cuda") if trans_b else torch.randn(k, n, device="cuda")
+    precision.set_precision(mode)
+    try:
+        out = gemm.matmul(a, b, trans_a=trans_a, trans_b=trans_b)
+    finally:
+        precision.set_precision("fp32")
+    torch.cuda.synchronize()
+    check_status()
+    ref = _ref(a, b, trans_a, trans_b)
+    err = _rel_err(out, ref)
+    if mode == "tf32":
+        tol = 2e-3
+    else:
+        # 3xTF32 must be within a small factor of true fp32 SGEMM accuracy.
+        torch.backends.cuda.matmul.allow_tf32 = False
+        lhs = a.t() if trans_a else a
+        rhs = b.t() if trans_b else b
+        tol = 8 * _rel_err(lhs @ rhs, ref) + 1e-6
+    assert err < tol, f"{mode} {shape} ta={trans_a} tb={trans_b}: rel err {err:.3e} (tol {tol:.3e})"
+
+
+def test_fp32_mode_matches_sgemm_accuracy():
+    torch.manual_seed(1)
+    a = torch.randn(512, 768, device="cuda")
+    b = torch.randn(768, 2048, device="cuda")
+    ref = _ref(a, b, False, False)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    sgemm_err = _rel_err(a @ b, ref)
+    out = gemm.matmul(a, b)
+    ours = _rel_err(out, ref)
+    assert ours < 4 * sgemm_err + 1e-7, f"3xTF32 err {ours:.3e} vs SGEMM {sgemm_err:.3e}"
+
+
+def test_gemm_epilogue_residual_accumulate_alpha():
+    torch.manual_seed(2)
+    a = torch.randn(300, 256, device="cuda")
+    b = torch.randn(256, 384, device="cuda")
+    r = torch.randn(300, 384, device="cuda")
+    c0 = torch.randn(300, 384, device="cuda")
+    out = c0.clone()
+    gemm.matmul(a, b, alpha=0.5, residual=r, out=out, accumulate=True)
+    ref = 0.5 * _ref(a, b, False, False) + r.double() + c0.double()
+    assert _rel_err(out, ref) < 5e-6
+
+
+def test_gemm_segmented_n_and_k():
+    torch.manual_seed(3)
+    x = torch.randn(260, 768, device="cuda")
+    ws = [torch.randn(768, 768, device="cuda") for _ in range(3)]
+    out = gemm.matmul(x, ws, b_mode=gemm.B_SEG_N)
+    ref = x.double() @ torch.cat(ws, 1).double()
+    assert _rel_err(out, ref) < 5e-6
+    dq = torch.randn(260, 3 * 768, device="cuda")
+    out = gemm.matmul(dq, ws, trans_b=True, b_mode=gemm.B_SEG_K)
+    ref = dq.double() @ torch.cat([w.t() for w in ws], 0).double()
+    assert _rel_err(out, ref) < 5e-6
+
+
+@pytest.mark.parametrize("tokens,dim,hidden", [(256, 128, 256), (300, 256, 688), (1024, 768, 2048)])
+def test_swiglu_mlp_forward_backward(tokens, dim, hidden):
+    torch.manual_seed(4)
+    x = torch.randn(tokens, dim, device="cuda", requires_grad=True)
+    wg = (torch.randn(dim, hidden, device="cuda") / dim**0.5).requires_grad_()
+    wu = (torch.randn(dim, hidden, device="cuda") / dim**0.5).requires_grad_()
+    wd = (torch.randn(hidden, dim, device="cuda") / hidden**0.5).requires_grad_()
+    r = torch.randn(tokens, dim, device="cuda", requires_grad=True)
+    y = gemm.swiglu_mlp(x, wg, wu, wd, residual=r)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    leaves = [x, wg, wu, wd, r]
+    ours = [t.grad.clone() for t in leaves]
+    xd, wgd, wud, wdd, rd = [t.detach().double().requires_grad_() for t in leaves]
+    yd = rd + (torch.nn.functional.silu(xd @ wgd) * (xd @ wud)) @ wdd
+    yd.backward(gy.double())
+    assert _rel_err(y, yd.detach()) < 1e-5
+    for got, ref in zip(ours, [xd.grad, wgd.grad, wud.grad, wdd.grad, rd.grad]):
+        assert _rel_err(got, ref) < 1e-5
+
+
+def test_linear_autograd_matches_fp64():
+    torch.manual_seed(5)
+    x = torch.randn(4, 64, 256, device="cuda", requires_grad=True)
+    w = (torch.randn(256, 512, device="cuda") / 16).requires_grad_()
+    y = gemm.linear(x, w)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    xd, wd = x.detach().double().requires_grad_(), w.detach().double().requires_grad_()
+    (xd @ wd).backward(gy.double())
+    assert _rel_err(x.grad, xd.grad) < 1e-5
+    assert _rel_err(w.grad, wd.grad) < 1e-5

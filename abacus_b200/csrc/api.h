@@ -37,3 +37,15 @@ void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> gr
                 double weight_decay, int64_t step);
 }  // namespace ops
 }  // namespace abacus
+
+namespace abacus {
+namespace attn {
+void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                    int64_t batch, int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
+                    c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes);
+void flash_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor dout,
+                    torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, int64_t batch,
+                    int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
+                    c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes);
+}  // namespace attn
+}  // namespace abacus

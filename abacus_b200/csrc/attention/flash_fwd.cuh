@@ -1,0 +1,423 @@
+// Causal flash-attention forward on tcgen05 (kind::tf32), fp32 in / out.
+//
+// One CTA = 128 queries of one (batch, head). Keys are visited in blocks of
+// 64; blocks entirely in the masked future are skipped (positions may be the
+// global zigzag positions of context parallelism).
+//
+//   warp 0      TMA producer: Q once, then K_j / V_j into a 2-stage ring
+//   warp 1      TMEM allocator + single-thread MMA issuer
+//                 S_j  = Q K_j^T          (A, B from smem, K-major)
+//                 PV_j = P_j V_j          (A = P from TMEM, B = V MN-major)
+//   warps 2-5   softmax: one query row per thread. Reads S_j from TMEM,
+//               masks / scales, online max & sum, writes P_j into TMEM (the
+//               columns S_j came from), then folds PV_{j-1} into its fp32
+//               register accumulator with the online-softmax rescale.
+//   warps 6-9   (3xTF32 only) split converter: each landed Q / K / V tile is
+//               rewritten as hi (in place) and lo, so every product is
+//               lo*hi + hi*lo + hi*hi.
+//
+// P_j never touches shared or global memory, the (L, L) score matrix is never
+// materialised, and each PV_j lands in a fresh TMEM buffer that is added to
+// the register accumulator with round-to-nearest fp32 adds (the tensor core's
+// own accumulation spans one 64-key block only).
+//
+// TMEM columns: SP[2] (S, then P hi [+ P lo]) and PV[2].
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cfloat>
+#include <cstdint>
+#include "../common/sm100.cuh"
+
+namespace abacus {
+namespace attn {
+
+constexpr int kBlockM = 128;  // queries per CTA (one per softmax thread)
+constexpr int kBlockN = 64;   // keys per block
+
+struct FwdParams {
+  CUtensorMap tma_q;   // box {32, 128} over (B*Lq, ld_q), SWIZZLE_128B
+  CUtensorMap tma_k;   // box {32, 64}  over (B*Lk, ld_k), SWIZZLE_128B
+  CUtensorMap tma_v;   // box {32, 64}  over (B*Lk, ld_v), SWIZZLE_128B_ATOM_32B
+  float* out;          // (B*Lq, ld_o)
+  long long ld_o;
+  float* lse;          // (B, H, Lq)
+  const int64_t* q_pos;  // (Lq,) or null (then position = index)
+  const int64_t* k_pos;  // (Lk,) or null
+  int batch, heads, lq, lk;
+  float scale_log2;    // softmax scale * log2(e)
+  int* status;
+};
+
+template <int D, int PASSES>
+struct FwdCfg {
+  static constexpr int kQBytes = kBlockM * D * 4;
+  static constexpr int kKBytes = kBlockN * D * 4;
+  static constexpr int kVBytes = kBlockN * D * 4;
+  static constexpr int kSplit = PASSES == 3 ? 2 : 1;
+  static constexpr int kStages = 2;
+  static constexpr int kStageBytes = (kKBytes + kVBytes) * kSplit;
+  static constexpr int kSmemBytes = kQBytes * kSplit + kStages * kStageBytes + 1024;
+  static constexpr int kThreads = PASSES == 3 ? 320 : 192;
+  static constexpr int kSPCols = kBlockN * (PASSES == 3 ? 2 : 1);  // S / P hi [/ P lo]
+  static constexpr int kPVBase = 2 * kSPCols;
+  static constexpr int kCols = kPVBase + 2 * D;
+  static constexpr uint32_t kTmemCols = kCols <= 256 ? 256 : 512;
+  static constexpr int kMaxBlocks = 2048;  // key blocks per sequence (Lk <= 131072)
+};
+
+__device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
+
+template <int D, int PASSES>
+__global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kernel(const __grid_constant__ FwdParams p) {
+  using Cfg = FwdCfg<D, PASSES>;
+  static_assert(D % 32 == 0 && D <= 128, "head_dim must be 32, 64, 96 or 128");
+  static_assert(Cfg::kCols <= 512, "TMEM budget");
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t q_full, q_conv;
+  __shared__ uint64_t kv_full[2], kv_conv[2], kv_empty[2];
+  __shared__ uint64_t s_full[2], p_full[2], pv_full[2], pv_empty[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int n_blocks;
+  __shared__ int block_list[Cfg::kMaxBlocks];  // key block index | (needs_mask << 30)
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // Abort early (uniformly for the whole CTA) if an earlier kernel on this
+  // device already recorded an error.
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) abort_flag = *reinterpret_cast<volatile int*>(p.status);
+  __syncthreads();
+  if (abort_flag != kStatusOk) return;
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sq = smem;                                   // Q hi [| Q lo]
+  uint8_t* skv = smem + Cfg::kQBytes * Cfg::kSplit;     // stages: K hi, V hi [, K lo, V lo]
+  auto k_hi = [&](int s) { return skv + s * Cfg::kStageBytes; };
+  auto v_hi = [&](int s) { return skv + s * Cfg::kStageBytes + Cfg::kKBytes; };
+  auto k_lo = [&](int s) { return skv + s * Cfg::kStageBytes + Cfg::kKBytes + Cfg::kVBytes; };
+  auto v_lo = [&](int s) { return skv + s * Cfg::kStageBytes + 2 * Cfg::kKBytes + Cfg::kVBytes; };
+
+  // Heavy (late) query blocks first: causal work grows with the block index.
+  const int num_mb = (p.lq + kBlockM - 1) / kBlockM;
+  const int mb = num_mb - 1 - blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int m0 = mb * kBlockM;
+  const int q_row0 = b * p.lq + m0;  // row in the (B*Lq) matrix
+  const int k_row0 = b * p.lk;
+  const int col0 = h * D;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    mbar_init(&q_conv, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_conv[i], 128);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_full[i], 1);
+      mbar_init(&pv_empty[i], 128);
+    }
+    fence_mbar_init();
+  }
+  // Key blocks this query block must visit, with a flag for blocks that
+  // straddle the causal boundary (need per-element masking).
+  if (warp == 0) {
+    // Query position range of this block.
+    int qmin = INT_MAX, qmax = INT_MIN;
+    for (int i = lane; i < kBlockM; i += 32) {
+      const int qi = m0 + i;
+      if (qi < p.lq) {
+        const int pos = p.q_pos ? static_cast<int>(p.q_pos[qi]) : qi;
+        qmin = min(qmin, pos);
+        qmax = max(qmax, pos);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      qmin = min(qmin, __shfl_xor_sync(0xffffffffu, qmin, o));
+      qmax = max(qmax, __shfl_xor_sync(0xffffffffu, qmax, o));
+    }
+    const int nkb = (p.lk + kBlockN - 1) / kBlockN;
+    int count = 0;
+    for (int base = 0; base < nkb; base += 32) {
+      const int kb = base + lane;
+      bool keep = false, partial = false;
+      if (kb < nkb) {
+        int kmin = INT_MAX, kmax = INT_MIN;
+        for (int i = 0; i < kBlockN; ++i) {
+          const int ki = kb * kBlockN + i;
+          if (ki < p.lk) {
+            const int pos = p.k_pos ? static_cast<int>(p.k_pos[ki]) : ki;
+            kmin = min(kmin, pos);
+            kmax = max(kmax, pos);
+          }
+        }
+        keep = kmin <= qmax;
+        partial = kmax > qmin || (kb * kBlockN + kBlockN > p.lk);
+      }
+      const unsigned keep_mask = __ballot_sync(0xffffffffu, keep);
+      if (keep) {
+        const int slot = count + __popc(keep_mask & ((1u << lane) - 1u));
+        if (slot < Cfg::kMaxBlocks) block_list[slot] = kb | (partial ? (1 << 30) : 0);
+      }
+      count += __popc(keep_mask);
+    }
+    if (lane == 0) n_blocks = min(count, Cfg::kMaxBlocks);
+    if (lane == 0 && count > Cfg::kMaxBlocks) atomicCAS(p.status, kStatusOk, kStatusBadArgs);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const int nb = n_blocks;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (elect_one_sync()) {
+      tma_prefetch_desc(&p.tma_q);
+      tma_prefetch_desc(&p.tma_k);
+      tma_prefetch_desc(&p.tma_v);
+      mbar_arrive_expect_tx(&q_full, Cfg::kQBytes);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) tma_load_2d(sq + c * kBlockM * 128, &p.tma_q, &q_full, col0 + 32 * c, q_row0);
+      int issued = 0;
+      for (int j = 0; j < nb; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+        const int kb = block_list[j] & 0xFFFF;
+        const int krow = k_row0 + kb * kBlockN;
+        mbar_arrive_expect_tx(&kv_full[s], Cfg::kKBytes + Cfg::kVBytes);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          tma_load_2d(k_hi(s) + c * kBlockN * 128, &p.tma_k, &kv_full[s], col0 + 32 * c, krow);
+          tma_load_2d(v_hi(s) + c * kBlockN * 128, &p.tma_v, &kv_full[s], col0 + 32 * c, krow);
+        }
+        ++issued;
+      }
+      mbar_wait(&q_full, 0, nullptr, 0);
+      for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc_s = idesc_tf32(kBlockM, kBlockN, false, false);
+      constexpr uint32_t idesc_pv = idesc_tf32(kBlockM, D, false, true);
+      bool ok = mbar_wait(PASSES == 3 ? &q_conv : &q_full, 0, p.status, kStatusTimeoutFull);
+      // S_j = Q K_j^T into SP[j & 1].
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(PASSES == 3 ? &kv_conv[s] : &kv_full[s], (j >> 1) & 1, p.status, kStatusTimeoutFull))
+          return false;
+        tc_fence_after();
+        const uint32_t d = tmem + s * Cfg::kSPCols;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t qa = smem_u32(sq) + c * kBlockM * 128 + ks * 32;
+            const uint32_t kb = smem_u32(k_hi(s)) + c * kBlockN * 128 + ks * 32;
+            const uint32_t acc = (c | ks) ? 1u : 0u;
+            if (PASSES == 3) {
+              const uint32_t ql = qa + Cfg::kQBytes;
+              const uint32_t kl = kb + (Cfg::kKBytes + Cfg::kVBytes);
+              mma_tf32_ss(d, desc_kmajor_sw128(ql), desc_kmajor_sw128(kb), idesc_s, acc);
+              mma_tf32_ss(d, desc_kmajor_sw128(qa), desc_kmajor_sw128(kl), idesc_s, 1u);
+              mma_tf32_ss(d, desc_kmajor_sw128(qa), desc_kmajor_sw128(kb), idesc_s, 1u);
+            } else {
+              mma_tf32_ss(d, desc_kmajor_sw128(qa), desc_kmajor_sw128(kb), idesc_s, acc);
+            }
+          }
+        }
+        mma_commit(&s_full[s]);
+        return true;
+      };
+      // PV_j = P_j V_j into PV[j & 1].
+      auto issue_pv = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&p_full[s], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) return false;
+        if (j >= 2 && !mbar_wait(&pv_empty[s], ((j >> 1) - 1) & 1, p.status, kStatusTimeoutAccum)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + Cfg::kPVBase + s * D;
+        const uint32_t p_hi = tmem + s * Cfg::kSPCols;
+        const uint32_t v_base = smem_u32(v_hi(s));
+#pragma unroll
+        for (int ks = 0; ks < kBlockN / 8; ++ks) {
+          const uint64_t vb = desc_mnmajor_sw128_32b(v_base + ks * 1024, kBlockN * 128);
+          const uint32_t acc = ks ? 1u : 0u;
+          if (PASSES == 3) {
+            const uint64_t vl = desc_mnmajor_sw128_32b(v_base + Cfg::kKBytes + Cfg::kVBytes + ks * 1024, kBlockN * 128);
+            mma_tf32_ts(d, p_hi + kBlockN + ks * 8, vb, idesc_pv, acc);  // P lo * V hi
+            mma_tf32_ts(d, p_hi + ks * 8, vl, idesc_pv, 1u);             // P hi * V lo
+            mma_tf32_ts(d, p_hi + ks * 8, vb, idesc_pv, 1u);             // P hi * V hi
+          } else {
+            mma_tf32_ts(d, p_hi + ks * 8, vb, idesc_pv, acc);
+          }
+        }
+        mma_commit(&pv_full[s]);
+        mma_commit(&kv_empty[s]);
+        return true;
+      };
+      for (int j = 0; j < nb && ok; ++j) {
+        ok = issue_s(j);
+        if (ok && j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok && nb >= 1) ok = issue_pv(nb - 1);
+      // Drain: every commit lands before this CTA releases its shared memory.
+      if (nb >= 1) {
+        for (int j = max(0, nb - 2); j < nb; ++j) mbar_wait(&kv_empty[j & 1], (j >> 1) & 1, p.status, kStatusTimeoutEmpty);
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- softmax
+    const int q = warp % 4;
+    const int r = q * 32 + lane;  // row within the block == TMEM lane
+    const int qi = m0 + r;
+    const int qpos = qi < p.lq ? (p.q_pos ? static_cast<int>(p.q_pos[qi]) : qi) : INT_MIN;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    float o[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    float m = -FLT_MAX, l = 0.f, alpha_prev = 0.f;
+    bool ok = true;
+    for (int j = 0; j <= nb && ok; ++j) {
+      float alpha = 1.f;
+      if (j < nb) {
+        const int s = j & 1;
+        const int entry = block_list[j];
+        const int kb = entry & 0xFFFF;
+        const bool partial = (entry >> 30) & 1;
+        if (!mbar_wait_warp(&s_full[s], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // Scaled, masked scores of 32 columns of S_j (re-read from TMEM, which
+        // is cheaper than keeping 64 scores live in registers).
+        auto load_scores = [&](int c, float (&sv)[32]) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + s * Cfg::kSPCols + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(v[i]) * p.scale_log2;
+          if (partial) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int ki = kb * kBlockN + c * 32 + i;
+              const bool valid = ki < p.lk && (p.k_pos ? static_cast<int>(__ldg(p.k_pos + ki)) : ki) <= qpos;
+              if (!valid) sv[i] = -FLT_MAX;
+            }
+          }
+        };
+        float bmax = -FLT_MAX;
+#pragma unroll
+        for (int c = 0; c < kBlockN / 32; ++c) {
+          float sv[32];
+          load_scores(c, sv);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) bmax = fmaxf(bmax, sv[i]);
+        }
+        const float m_new = fmaxf(m, bmax);
+        alpha = (m == -FLT_MAX) ? 0.f : fast_exp2(m - m_new);
+        float bsum = 0.f;
+        // P into the TMEM columns S came from (and the next kBlockN for P lo).
+#pragma unroll
+        for (int c = 0; c < kBlockN / 32; ++c) {
+          float sv[32];
+          load_scores(c, sv);
+          uint32_t vh[32];
+          uint32_t vl[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float e = (sv[i] == -FLT_MAX) ? 0.f : fast_exp2(sv[i] - m_new);
+            bsum += e;
+            if (PASSES == 3) {
+              const float hi = to_tf32(e);
+              vh[i] = __float_as_uint(hi);
+              vl[i] = __float_as_uint(to_tf32(e - hi));
+            } else {
+              vh[i] = __float_as_uint(e);
+            }
+          }
+          tmem_st32(lane_base + s * Cfg::kSPCols + c * 32, vh);
+          if (PASSES == 3) tmem_st32(lane_base + s * Cfg::kSPCols + kBlockN + c * 32, vl);
+        }
+        l = l * alpha + bsum;
+        m = m_new;
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[s]);
+      }
+      if (j >= 1) {
+        // Fold PV_{j-1}: o = o * alpha_{j-1} + PV_{j-1}.
+        const int s = (j - 1) & 1;
+        if (!mbar_wait_warp(&pv_full[s], ((j - 1) >> 1) & 1, p.status, kStatusTimeoutAccum)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + Cfg::kPVBase + s * D + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + __uint_as_float(v[i]);
+        }
+        tc_fence_before();
+        mbar_arrive(&pv_empty[s]);
+      }
+      alpha_prev = alpha;
+    }
+    if (ok && qi < p.lq) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      float* orow = p.out + static_cast<long long>(q_row0 + r) * p.ld_o + col0;
+#pragma unroll
+      for (int i = 0; i < D; i += 4)
+        *reinterpret_cast<float4*>(orow + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+      // Natural-log LSE of the scaled scores.
+      p.lse[(static_cast<long long>(b) * p.heads + h) * p.lq + qi] = (m + log2f(l)) * 0.69314718055994531f;
+    }
+  } else if (PASSES == 3) {
+    // ---------------------------------------------------------------- converter
+    const int ct = threadIdx.x - 192;
+    auto split = [&](uint8_t* hi_buf, uint8_t* lo_buf, int bytes) {
+      float4* hi = reinterpret_cast<float4*>(hi_buf);
+      float4* lo = reinterpret_cast<float4*>(lo_buf);
+      for (int i = ct; i < bytes / 16; i += 128) {
+        const float4 x = hi[i];
+        const float4 a = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
+        hi[i] = a;
+        lo[i] = make_float4(to_tf32(x.x - a.x), to_tf32(x.y - a.y), to_tf32(x.z - a.z), to_tf32(x.w - a.w));
+      }
+    };
+    bool ok = mbar_wait_warp(&q_full, 0, p.status, kStatusTimeoutFull);
+    if (ok) {
+      split(sq, sq + Cfg::kQBytes, Cfg::kQBytes);
+      fence_proxy_async_smem();
+      mbar_arrive(&q_conv);
+    }
+    for (int j = 0; j < nb && ok; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait_warp(&kv_full[s], (j >> 1) & 1, p.status, kStatusTimeoutFull)) break;
+      split(k_hi(s), k_lo(s), Cfg::kKBytes);
+      split(v_hi(s), v_lo(s), Cfg::kVBytes);
+      fence_proxy_async_smem();
+      mbar_arrive(&kv_conv[s]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace attn
+}  // namespace abacus

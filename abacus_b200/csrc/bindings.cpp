@@ -16,6 +16,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_fwd_bwd", &abacus::ops::cross_entropy_fwd_bwd);
   m.def("cross_entropy_grad", &abacus::ops::cross_entropy_grad);
   m.def("adamw_step", &abacus::ops::adamw_step);
+  m.def("flash_attn_fwd", &abacus::attn::flash_attn_fwd);
+  m.def("flash_attn_bwd", &abacus::attn::flash_attn_bwd);
+  m.def("launch_count", &abacus::host::launch_count, "number of abacus kernels launched by this process");
   m.def("read_status", &abacus::host::read_status, "device status word (0 = healthy)");
   m.def("reset_status", &abacus::host::reset_status, "clear the device status word");
 }

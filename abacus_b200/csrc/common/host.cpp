@@ -6,6 +6,13 @@ namespace abacus {
 namespace host {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+  thread_local int bound_device = -1;
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  if (bound_device != dev) {
+    C10_CUDA_CHECK(cudaSetDevice(dev));  // makes the primary context current on this thread
+    bound_device = dev;
+  }
   static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -17,6 +24,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
 }
 
 namespace {
+std::atomic<long long> g_launches{0};
 std::mutex g_mu;
 int* g_status[64] = {nullptr};
 }  // namespace
@@ -34,6 +42,9 @@ int* status_ptr(int device) {
   }
   return g_status[device];
 }
+
+void note_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 int read_status(int device) {
   int v = 0;

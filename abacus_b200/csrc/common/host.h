@@ -13,7 +13,9 @@ namespace abacus {
 namespace host {
 
 // cuTensorMapEncodeTiled, fetched through the runtime so the extension does not
-// link libcuda directly.
+// link libcuda directly. Also binds the current device's primary context to
+// the calling thread (driver-API calls need a current context, which threads
+// such as the autograd engine's workers may not have yet).
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled();
 
 // Device pointer to this device's status word (zero = healthy). Kernels record
@@ -21,6 +23,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled();
 int* status_ptr(int device);
 int read_status(int device);
 void reset_status(int device);
+
+// Number of abacus kernels launched by this process (every launch site calls
+// note_launch right after its <<<>>>), so benchmarks can report how many of
+// the timed region's kernels are this library's own.
+void note_launch(int n = 1);
+long long launch_count();
 
 // Runs `fn` once per CUDA device (the current one).
 class PerDeviceOnce {

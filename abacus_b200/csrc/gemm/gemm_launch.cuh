@@ -20,6 +20,7 @@ void launch_t(const Params& p, int grid, cudaStream_t stream) {
   });
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
 }
 
 template <int BN, int EPI>

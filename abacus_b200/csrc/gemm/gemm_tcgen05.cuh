@@ -90,7 +90,12 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  if (*reinterpret_cast<volatile int*>(p.status) != kStatusOk) return;
+  // Abort early (uniformly for the whole CTA) if an earlier kernel on this
+  // device already recorded an error.
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) abort_flag = *reinterpret_cast<volatile int*>(p.status);
+  __syncthreads();
+  if (abort_flag != kStatusOk) return;
 
   // 1024-byte aligned stage buffers (swizzle period of SWIZZLE_128B).
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -269,7 +274,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
       const int num_chunks = (num_k + Cfg::kChunk - 1) / Cfg::kChunk;
       for (int j = 0; j < num_chunks && ok; ++j) {
         const int buf = j & 1;
-        if (!mbar_wait(&chunk_full[buf], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) {
+        if (!mbar_wait_warp(&chunk_full[buf], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) {
           ok = false;
           break;
         }
@@ -286,7 +291,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
         mbar_arrive(&chunk_empty[buf]);
       }
     } else {
-      ok = ok && mbar_wait(&accum_bar, 0, p.status, kStatusTimeoutAccum);
+      ok = mbar_wait_warp(&accum_bar, 0, p.status, kStatusTimeoutAccum) && ok;
       tc_fence_after();
     }
     // Fetch the 32 accumulator columns of group c.
@@ -387,7 +392,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     for (int kt = 0; kt < num_k; ++kt) {
       const int s = kt % STAGES;
       const int use = kt / STAGES;
-      if (!mbar_wait(&full_bar[s], use & 1, p.status, kStatusTimeoutFull)) break;
+      if (!mbar_wait_warp(&full_bar[s], use & 1, p.status, kStatusTimeoutFull)) break;
       // A and B hi/lo regions are each contiguous; swizzling only permutes
       // positions, so an elementwise pass over the bytes is layout-agnostic.
       float4* a = reinterpret_cast<float4*>(stage_a(s));

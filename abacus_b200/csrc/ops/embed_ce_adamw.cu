@@ -7,6 +7,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <cfloat>
 #include "../api.h"
+#include "../common/host.h"
 
 namespace abacus {
 namespace ops {
@@ -225,6 +226,7 @@ void embedding_fwd(torch::Tensor tokens, torch::Tensor weight, torch::Tensor out
       tokens.data_ptr<int64_t>(), weight.data_ptr<float>(), out.data_ptr<float>(), n, static_cast<int>(weight.size(1)),
       weight.size(0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
 }
 
 void embedding_bwd(torch::Tensor sorted_tokens, torch::Tensor perm, torch::Tensor dy, torch::Tensor dw) {
@@ -237,6 +239,7 @@ void embedding_bwd(torch::Tensor sorted_tokens, torch::Tensor perm, torch::Tenso
       sorted_tokens.data_ptr<int64_t>(), perm.data_ptr<int64_t>(), dy.data_ptr<float>(), dw.data_ptr<float>(), n,
       static_cast<int>(dw.size(1)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
 }
 
 void cross_entropy_fwd_bwd(torch::Tensor logits, torch::Tensor target, torch::Tensor loss, c10::optional<torch::Tensor> lse,
@@ -253,6 +256,7 @@ void cross_entropy_fwd_bwd(torch::Tensor logits, torch::Tensor target, torch::Te
       lse ? lse->data_ptr<float>() : nullptr, static_cast<int>(logits.size(1)), ignore_index,
       grad_scale.data_ptr<float>(), write_grad ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
 }
 
 void cross_entropy_grad(torch::Tensor logits, torch::Tensor grad, torch::Tensor target, torch::Tensor lse,
@@ -266,6 +270,7 @@ void cross_entropy_grad(torch::Tensor logits, torch::Tensor grad, torch::Tensor 
       logits.data_ptr<float>(), logits.stride(0), grad.data_ptr<float>(), grad.stride(0), target.data_ptr<int64_t>(),
       lse.data_ptr<float>(), static_cast<int>(logits.size(1)), ignore_index, grad_scale.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
 }
 
 void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> grads, std::vector<torch::Tensor> exp_avgs,
@@ -305,6 +310,7 @@ void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> gr
     adamw_kernel<<<blocks, 256, 0, stream>>>(b, static_cast<float>(lr), static_cast<float>(beta1), static_cast<float>(beta2),
                                              static_cast<float>(eps), static_cast<float>(weight_decay), bc1, bc2_sqrt);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
   }
 }
 

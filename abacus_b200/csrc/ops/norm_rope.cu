@@ -9,6 +9,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include "../api.h"
+#include "../common/host.h"
 
 namespace abacus {
 namespace ops {
@@ -61,7 +62,6 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const float* _
                                                                  const float* __restrict__ gamma, const float* __restrict__ rstd,
                                                                  float* __restrict__ dx, float* __restrict__ partial, int rows,
                                                                  int dim, int rows_per_block) {
-  extern __shared__ float sh_dg[];  // kWarps x dim
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n4 = dim / 4;
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
@@ -102,18 +102,12 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const float* _
                                r * gd[i].w - xv[i].w * c);
     }
   }
-  // Block-level partial of dgamma: warps -> smem -> one row per block.
+  // Per-warp partial rows of dgamma (reduced by reduce_partials_kernel).
+  float4* prow = reinterpret_cast<float4*>(partial + (static_cast<long long>(blockIdx.x) * kWarps + warp) * dim);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int idx = lane + 32 * i;
-    if (idx < n4) reinterpret_cast<float4*>(sh_dg + warp * dim)[idx] = acc[i];
-  }
-  __syncthreads();
-  for (int j = threadIdx.x; j < dim; j += blockDim.x) {
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) s += sh_dg[w * dim + j];
-    partial[static_cast<long long>(blockIdx.x) * dim + j] = s;
+    if (idx < n4) prow[idx] = acc[i];
   }
 }
 
@@ -296,6 +290,7 @@ void rmsnorm_fwd(torch::Tensor x, torch::Tensor gamma, torch::Tensor y, torch::T
   else LAUNCH(32);
 #undef LAUNCH
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
 }
 
 void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor gamma, torch::Tensor rstd, torch::Tensor dx,
@@ -309,10 +304,10 @@ void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor gamma, torch::
   }
   const int nblocks = partial_blocks(x.device(), (rows + kWarps - 1) / kWarps);
   const int rows_per_block = (rows + nblocks - 1) / nblocks;
-  auto partial = torch::empty({nblocks, dim}, x.options());
+  auto partial = torch::empty({nblocks * kWarps, dim}, x.options());
   auto s = at::cuda::getCurrentCUDAStream();
   const int vpl = (dim / 4 + 31) / 32;
-  const size_t smem = kWarps * dim * sizeof(float);
+  const size_t smem = 0;
 #define LAUNCH(V)                                                                                                   \
   rmsnorm_bwd_kernel<V><<<nblocks, kWarps * 32, smem, s>>>(dy.data_ptr<float>(), x.data_ptr<float>(),                \
                                                           gamma.data_ptr<float>(), rstd.data_ptr<float>(),         \
@@ -325,8 +320,11 @@ void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor gamma, torch::
   else LAUNCH(32);
 #undef LAUNCH
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  reduce_partials_kernel<<<(dim + 255) / 256, 256, 0, s>>>(partial.data_ptr<float>(), dgamma.data_ptr<float>(), nblocks, dim);
+  abacus::host::note_launch();
+  reduce_partials_kernel<<<(dim + 255) / 256, 256, 0, s>>>(partial.data_ptr<float>(), dgamma.data_ptr<float>(),
+                                                           nblocks * kWarps, dim);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
 }
 
 void qk_prologue_fwd(torch::Tensor qkv, torch::Tensor gq, torch::Tensor gk, torch::Tensor cos_t, torch::Tensor sin_t,
@@ -352,6 +350,7 @@ void qk_prologue_fwd(torch::Tensor qkv, torch::Tensor gq, torch::Tensor gk, torc
   else LAUNCH(4);
 #undef LAUNCH
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
 }
 
 void qk_prologue_bwd(torch::Tensor qkv, torch::Tensor gq, torch::Tensor gk, torch::Tensor cos_t, torch::Tensor sin_t,
@@ -384,10 +383,12 @@ void qk_prologue_bwd(torch::Tensor qkv, torch::Tensor gq, torch::Tensor gk, torc
   else LAUNCH(4);
 #undef LAUNCH
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
   auto sums = torch::empty({2 * head_dim}, qkv.options());
   reduce_partials_kernel<<<static_cast<int>((2 * head_dim + 255) / 256), 256, 0, s>>>(
       partial.data_ptr<float>(), sums.data_ptr<float>(), nblocks, static_cast<int>(2 * head_dim));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
   dgq.copy_(sums.narrow(0, 0, head_dim));
   dgk.copy_(sums.narrow(0, head_dim, head_dim));
 }

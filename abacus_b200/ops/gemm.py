@@ -138,7 +138,12 @@ class _SwiGLU(torch.autograd.Function):
         hidden = w_gate.shape[1]
         dgu = torch.empty(g2.shape[0], 2 * hidden, device=g2.device, dtype=torch.float32)
         ext().gemm_swiglu_bwd(g2, w_down, g, u, dgu, precision.passes())
-        grad_x = matmul(dgu, [w_gate, w_up], trans_b=True, b_mode=B_SEG_K).reshape(ctx.x_shape)
+        if hidden % 32 == 0:
+            grad_x = matmul(dgu, [w_gate, w_up], trans_b=True, b_mode=B_SEG_K)
+        else:  # K segments must be whole 32-element k-tiles: two accumulating GEMMs
+            grad_x = matmul(dgu[:, :hidden], w_gate, trans_b=True)
+            matmul(dgu[:, hidden:], w_up, trans_b=True, out=grad_x, accumulate=True)
+        grad_x = grad_x.reshape(ctx.x_shape)
         grad_wg = matmul(x2, dgu[:, :hidden], trans_a=True)
         grad_wu = matmul(x2, dgu[:, hidden:], trans_a=True)
         grad_wd = matmul(h, g2, trans_a=True)

@@ -60,12 +60,13 @@ class Trainer:
         weight_decay: float = 1e-2,
         schedule_lr: float = 5e-4,
         print_memory: bool = False,
+        device: torch.device | str | None = None,
     ):
         if parallel is not None and pipeline is not None and mesh.get_mesh() is None:
             raise ValueError("pipeline parallel does not use DataParallel")
         if pipeline is not None and getattr(model, "context_parallel", False) and mesh.get_mesh() is None:
             raise ValueError("pipeline parallel does not combine with context parallel")
-        self.device = get_device()
+        self.device = get_device() if device is None else torch.device(device)
         self.model = model.to(self.device)
         self.parallel = parallel
         self.pipeline = pipeline

@@ -11,6 +11,13 @@ from setuptools import setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+
+# Link libstdc++ dynamically: a toolchain that silently falls back to the
+# static archive puts a second libstdc++ into the process next to torch's, and
+# stream formatting (e.g. error messages) then crashes on non-main threads.
+for var, exe in (("CXX", "/usr/bin/g++"), ("CC", "/usr/bin/gcc")):
+    if os.path.exists(exe):
+        os.environ[var] = exe
 CSRC = os.path.join("abacus_b200", "csrc")
 
 sources = sorted(

@@ -20,7 +20,7 @@ def _rel_err(out, ref):
     return ((out.double() - ref).abs().max() / ref.abs().max()).item()
 
 
-SHAPES = [(128, 128, 32), (256, 256, 64), (200, 136, 72), (384, 512, 768), (1000, 2304, 768), (130, 300, 1028)]
+SHAPES = [(128, 128, 32), (256, 256, 64), (200, 136, 72), (384, 512, 768), (1000, 2304, 768), (132, 300, 1028)]
 
 
 @pytest.mark.parametrize("mode", ["tf32", "fp32"])

@@ -9,6 +9,9 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include "../api.h"
+#include "rmsnorm_noalloc.h"
+#include <algorithm>
+#include <mutex>
 #include "../common/host.h"
 
 namespace abacus {
@@ -395,3 +398,87 @@ void qk_prologue_bwd(torch::Tensor qkv, torch::Tensor gq, torch::Tensor gk, torc
 
 }  // namespace ops
 }  // namespace abacus
+
+// ============================================================================
+// Allocation-free RMSNorm backward (C ABI). Declared in rmsnorm_noalloc.h.
+//
+// The backward above reduces dgamma through a scratch buffer of per-warp
+// partial rows that it allocates on every call. This variant runs the same two
+// kernels but keeps that scratch in a fixed file-scope device array, so the
+// call performs no device allocation at all.
+// ============================================================================
+namespace abacus {
+namespace ops {
+namespace {
+
+// Scratch for the dgamma partial rows: (blocks * kWarps) rows of `dim` floats.
+constexpr long long kNoAllocScratchFloats = 1LL << 20;  // 4 MiB per GPU
+static __device__ __align__(256) float g_rmsnorm_noalloc_scratch[kNoAllocScratchFloats];
+
+// Device address of the scratch array, looked up once per device.
+float* g_scratch_addr[64] = {nullptr};
+int g_sm_count[64] = {0};
+std::mutex g_noalloc_mu;
+
+int noalloc_setup(int device) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_scratch_addr[device] != nullptr) return 0;
+  // Host code cannot use the array's name as a device address: ask the
+  // runtime for it, with `device` current.
+  void* ptr = nullptr;
+  cudaError_t err = cudaGetSymbolAddress(&ptr, g_rmsnorm_noalloc_scratch);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  int sms = 0;
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  g_sm_count[device] = sms;
+  g_scratch_addr[device] = static_cast<float*>(ptr);
+  return 0;
+}
+
+}  // namespace
+}  // namespace ops
+}  // namespace abacus
+
+extern "C" __attribute__((visibility("default"))) int abacus_rmsnorm_bwd_noalloc(
+    const float* dy, const float* x, const float* gamma, const float* rstd, float* dx, float* dgamma, int rows,
+    int dim, void* stream) {
+  using namespace abacus::ops;
+  if (rows < 0 || dim <= 0 || dim % 4 != 0 || dim > 4096) return ABACUS_NOALLOC_EBADSIZE;
+  if (dy == nullptr || x == nullptr || gamma == nullptr || rstd == nullptr || dx == nullptr || dgamma == nullptr)
+    return ABACUS_NOALLOC_EBADSIZE;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  if (device < 0 || device >= 64) return ABACUS_NOALLOC_EBADSIZE;
+  if (g_scratch_addr[device] == nullptr) {
+    const int rc = noalloc_setup(device);
+    if (rc != 0) return rc;
+  }
+  float* scratch = g_scratch_addr[device];
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Partial rows that fit in the scratch array; at least one block.
+  const long long max_blocks = kNoAllocScratchFloats / (static_cast<long long>(kWarps) * dim);
+  if (max_blocks < 1) return ABACUS_NOALLOC_EBADSIZE;
+  const long long want = std::max<long long>(1, std::min<long long>((rows + kWarps - 1) / kWarps, 4LL * g_sm_count[device]));
+  const int nblocks = static_cast<int>(std::min(want, max_blocks));
+  const int rows_per_block = rows == 0 ? 0 : (rows + nblocks - 1) / nblocks;
+  const int vpl = (dim / 4 + 31) / 32;
+  // Every partial row read below is written by this call (idle warps write
+  // zeros), so the scratch needs no clearing between calls.
+#define ABACUS_NOALLOC_LAUNCH(V)                                                                                  \
+  rmsnorm_bwd_kernel<V><<<nblocks, kWarps * 32, 0, s>>>(dy, x, gamma, rstd, dx, scratch, rows, dim, rows_per_block)
+  if (vpl <= 2) ABACUS_NOALLOC_LAUNCH(2);
+  else if (vpl <= 4) ABACUS_NOALLOC_LAUNCH(4);
+  else if (vpl <= 8) ABACUS_NOALLOC_LAUNCH(8);
+  else if (vpl <= 16) ABACUS_NOALLOC_LAUNCH(16);
+  else ABACUS_NOALLOC_LAUNCH(32);
+#undef ABACUS_NOALLOC_LAUNCH
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return static_cast<int>(err);
+  reduce_partials_kernel<<<(dim + 255) / 256, 256, 0, s>>>(scratch, dgamma, nblocks * kWarps, dim);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return static_cast<int>(err);
+  abacus::host::note_launch(2);
+  return 0;
+}

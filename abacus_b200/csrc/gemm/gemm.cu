@@ -4,6 +4,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include "gemm_launch.cuh"
 #include "../common/host.h"
 #include "../api.h"
@@ -63,6 +64,44 @@ Operand operand_of(const torch::Tensor& t, bool transposed_storage, const char* 
 CUtensorMap map_for(const Operand& o, int tile_mn) {
   if (o.mn_major) return make_map(o.ptr, o.mn, o.k, o.ld, 32, BK, true);
   return make_map(o.ptr, o.k, o.mn, o.ld, BK, tile_mn, false);
+}
+
+// C = alpha * sum_s ws[s] (+ residual) (+ C), summed in split order
+// (deterministic). ws: (splits, M, N) contiguous.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, long long M, long long N, float alpha,
+                                     const float* __restrict__ r, long long ldr, int accumulate, float* __restrict__ c,
+                                     long long ldc) {
+  const long long n4 = N / 4;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= M * n4) return;
+  const long long m = idx / n4, j = (idx % n4) * 4;
+  const long long plane = M * N;
+  float4 acc = *reinterpret_cast<const float4*>(ws + m * N + j);
+  for (int s = 1; s < splits; ++s) {
+    const float4 v = *reinterpret_cast<const float4*>(ws + s * plane + m * N + j);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  acc.x *= alpha; acc.y *= alpha; acc.z *= alpha; acc.w *= alpha;
+  if (r) {
+    const float4 v = *reinterpret_cast<const float4*>(r + m * ldr + j);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  float* cp = c + m * ldc + j;
+  if (accumulate) {
+    const float4 v = *reinterpret_cast<const float4*>(cp);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  *reinterpret_cast<float4*>(cp) = acc;
+}
+
+// Number of K splits for a GEMM with `tiles` output tiles and `k_tiles`
+// 32-deep k-tiles: enough CTAs for two waves, at least 32 k-tiles per split.
+int pick_splits(long long tiles, int k_tiles, int sms) {
+  if (tiles >= 2LL * sms || k_tiles < 64) return 1;
+  long long s = (2LL * sms + tiles - 1) / tiles;
+  s = std::min<long long>(s, 16);
+  s = std::min<long long>(s, k_tiles / 32);
+  return static_cast<int>(std::max<long long>(s, 1));
 }
 
 void check_passes(int64_t passes) { TORCH_CHECK(passes == 1 || passes == 3, "passes must be 1 (tf32) or 3 (3xTF32)"); }
@@ -132,9 +171,35 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
   }
   p.accumulate = accumulate ? 1 : 0;
   p.status = host::status_ptr(a.device().index());
-  const int grid = static_cast<int>(((M + BM - 1) / BM) * p.num_n_tiles);
+  const long long tiles = ((M + BM - 1) / BM) * p.num_n_tiles;
+  const int k_tiles = static_cast<int>((K + BK - 1) / BK);
+  const int sms = at::cuda::getDeviceProperties(a.device().index())->multiProcessorCount;
+  int splits = N % 4 == 0 ? pick_splits(tiles, k_tiles, sms) : 1;
   auto stream = at::cuda::getCurrentCUDAStream();
-  launch_store(p, grid, BN, A.mn_major, B[0].mn_major, static_cast<int>(passes), stream);
+  p.k_tiles_per_split = (k_tiles + splits - 1) / splits;
+  splits = (k_tiles + p.k_tiles_per_split - 1) / p.k_tiles_per_split;
+  if (splits == 1) {
+    launch_store(p, dim3(static_cast<unsigned>(tiles), 1), BN, A.mn_major, B[0].mn_major, static_cast<int>(passes),
+                 stream);
+    return;
+  }
+  // Split-K: partials into a workspace, then one deterministic reduction that
+  // also applies alpha / residual / accumulate.
+  auto ws = torch::empty({splits, M, N}, c.options());
+  Params q = p;
+  q.c = ws.data_ptr<float>();
+  q.ldc = N;
+  q.split_stride = M * N;
+  q.alpha = 1.f;
+  q.r = nullptr;
+  q.accumulate = 0;
+  launch_store(q, dim3(static_cast<unsigned>(tiles), static_cast<unsigned>(splits)), BN, A.mn_major, B[0].mn_major,
+               static_cast<int>(passes), stream);
+  const long long items = M * (N / 4);
+  splitk_reduce_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, stream>>>(
+      ws.data_ptr<float>(), splits, M, N, p.alpha, p.r, p.ldr, p.accumulate, p.c, p.ldc);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
 }
 
 // SwiGLU up-projection: g = x @ w_gate, u = x @ w_up, h = silu(g) * u.
@@ -170,9 +235,10 @@ void gemm_swiglu(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torc
   p.h = h.data_ptr<float>();
   p.ldh = h.stride(0);
   p.status = host::status_ptr(x.device().index());
+  p.k_tiles_per_split = static_cast<int>((A.k + BK - 1) / BK);
   const int grid = static_cast<int>(((T + BM - 1) / BM) * p.num_n_tiles);
   auto stream = at::cuda::getCurrentCUDAStream();
-  launch_swiglu(p, grid, BN, static_cast<int>(passes), stream);
+  launch_swiglu(p, dim3(grid, 1), BN, static_cast<int>(passes), stream);
 }
 
 // SwiGLU backward through the hidden layer: dh = dy @ w_down^T, then
@@ -206,9 +272,10 @@ void gemm_swiglu_bwd(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, to
   p.dgu = dgu.data_ptr<float>();
   p.ld_dgu = dgu.stride(0);
   p.status = host::status_ptr(dy.device().index());
+  p.k_tiles_per_split = static_cast<int>((A.k + BK - 1) / BK);
   const int grid = static_cast<int>(((T + BM - 1) / BM) * p.num_n_tiles);
   auto stream = at::cuda::getCurrentCUDAStream();
-  launch_swiglu_bwd(p, grid, BN, static_cast<int>(passes), stream);
+  launch_swiglu_bwd(p, dim3(grid, 1), BN, static_cast<int>(passes), stream);
 }
 
 }  // namespace gemm

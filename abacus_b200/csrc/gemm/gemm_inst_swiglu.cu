@@ -4,21 +4,21 @@
 namespace abacus {
 namespace gemm {
 
-void launch_store_128(const Params& p, int grid, bool a_mn, bool b_mn, int passes, cudaStream_t s);
-void launch_store_256(const Params& p, int grid, bool a_mn, bool b_mn, int passes, cudaStream_t s);
+void launch_store_128(const Params& p, dim3 grid, bool a_mn, bool b_mn, int passes, cudaStream_t s);
+void launch_store_256(const Params& p, dim3 grid, bool a_mn, bool b_mn, int passes, cudaStream_t s);
 
-void launch_store(const Params& p, int grid, int bn, bool a_mn, bool b_mn, int passes, cudaStream_t s) {
+void launch_store(const Params& p, dim3 grid, int bn, bool a_mn, bool b_mn, int passes, cudaStream_t s) {
   if (bn == 256) launch_store_256(p, grid, a_mn, b_mn, passes, s);
   else launch_store_128(p, grid, a_mn, b_mn, passes, s);
 }
 
-void launch_swiglu(const Params& p, int grid, int bn, int passes, cudaStream_t s) {
+void launch_swiglu(const Params& p, dim3 grid, int bn, int passes, cudaStream_t s) {
   TORCH_CHECK(bn == (passes == 3 ? 128 : 256), "SwiGLU tile width");
   if (passes == 3) launch_t<128, false, true, 3, kEpiSwiGLU>(p, grid, s);
   else launch_t<256, false, true, 1, kEpiSwiGLU>(p, grid, s);
 }
 
-void launch_swiglu_bwd(const Params& p, int grid, int bn, int passes, cudaStream_t s) {
+void launch_swiglu_bwd(const Params& p, dim3 grid, int bn, int passes, cudaStream_t s) {
   if (bn == 256) {
     TORCH_CHECK(passes == 1, "3xTF32 uses 128-column tiles");
     launch_t<256, false, false, 1, kEpiSwiGLUBwd>(p, grid, s);

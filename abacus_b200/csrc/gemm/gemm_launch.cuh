@@ -10,8 +10,8 @@ namespace abacus {
 namespace gemm {
 
 template <int BN, bool A_MN, bool B_MN, int PASSES, int EPI>
-void launch_t(const Params& p, int grid, cudaStream_t stream) {
-  constexpr int STAGES = PASSES == 3 ? (BN == 256 ? 2 : 3) : (BN == 256 ? 4 : 6);
+void launch_t(const Params& p, dim3 grid, cudaStream_t stream) {
+  constexpr int STAGES = PASSES == 3 ? 4 : (BN == 256 ? 4 : 6);
   using Cfg = Config<BN, A_MN, B_MN, PASSES, STAGES>;
   auto kern = gemm_kernel<BN, A_MN, B_MN, PASSES, EPI, STAGES>;
   static host::PerDeviceOnce once;
@@ -24,7 +24,7 @@ void launch_t(const Params& p, int grid, cudaStream_t stream) {
 }
 
 template <int BN, int EPI>
-void dispatch_layout(const Params& p, int grid, bool a_mn, bool b_mn, int passes, cudaStream_t s) {
+void dispatch_layout(const Params& p, dim3 grid, bool a_mn, bool b_mn, int passes, cudaStream_t s) {
 #define ABACUS_GEMM_CASE(AM, BMJ, PS) \
   if (a_mn == AM && b_mn == BMJ && passes == PS) return launch_t<BN, AM, BMJ, PS, EPI>(p, grid, s);
   ABACUS_GEMM_CASE(false, false, 1)
@@ -49,9 +49,9 @@ inline int pick_bn(long long n, int passes) {
 }
 
 // Defined in gemm_inst_*.cu.
-void launch_store(const Params& p, int grid, int bn, bool a_mn, bool b_mn, int passes, cudaStream_t s);
-void launch_swiglu(const Params& p, int grid, int bn, int passes, cudaStream_t s);
-void launch_swiglu_bwd(const Params& p, int grid, int bn, int passes, cudaStream_t s);
+void launch_store(const Params& p, dim3 grid, int bn, bool a_mn, bool b_mn, int passes, cudaStream_t s);
+void launch_swiglu(const Params& p, dim3 grid, int bn, int passes, cudaStream_t s);
+void launch_swiglu_bwd(const Params& p, dim3 grid, int bn, int passes, cudaStream_t s);
 
 }  // namespace gemm
 }  // namespace abacus

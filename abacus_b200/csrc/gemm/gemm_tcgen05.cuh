@@ -44,6 +44,10 @@ struct alignas(64) Params {
   const float* r;    // residual added by the store epilogue (nullable)
   long long ldr;
   int accumulate;    // store epilogue: C += result
+  // Split-K: CTA (tile, blockIdx.y) covers k-tiles [y * k_tiles_per_split, ...)
+  // and stores its fp32 partial at c + y * split_stride (reduced afterwards).
+  int k_tiles_per_split;
+  long long split_stride;
   // SwiGLU forward outputs (ld = ldh)
   float* g;
   float* u;
@@ -62,14 +66,17 @@ template <int BN, bool A_MN, bool B_MN, int PASSES, int STAGES>
 struct Config {
   static constexpr int kABytes = BM * BK * 4;
   static constexpr int kBBytes = BN * BK * 4;
-  static constexpr int kStageBytes = (kABytes + kBBytes) * (PASSES == 3 ? 2 : 1);
+  // 3xTF32 stage: A landing buffer, B hi (in place), B lo. A hi / lo live in
+  // TMEM (written by the converter), so the MMA reads A without touching smem.
+  static constexpr int kStageBytes = PASSES == 3 ? kABytes + 2 * kBBytes : kABytes + kBBytes;
   static constexpr int kSmemBytes = STAGES * kStageBytes + 1024;
   static constexpr int kThreads = PASSES == 3 ? 320 : 192;
   // 3xTF32 accumulates K in chunks of kChunk k-tiles into two alternating
   // TMEM buffers that the epilogue drains (see the epilogue).
   static constexpr bool kChunked = PASSES == 3;
   static constexpr int kChunk = 2;
-  static constexpr int kAccCols = kChunked ? 2 * BN : BN;
+  static constexpr int kATmem = 2 * BN;  // first TMEM column of the A stages (3xTF32)
+  static constexpr int kAccCols = kChunked ? 2 * BN + STAGES * 2 * BK : BN;
   static constexpr uint32_t kTmemCols = kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
 };
 
@@ -102,8 +109,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   auto stage_a = [&](int s) { return smem + s * Cfg::kStageBytes; };
   auto stage_b = [&](int s) { return smem + s * Cfg::kStageBytes + Cfg::kABytes; };
-  auto stage_alo = [&](int s) { return smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes; };
-  auto stage_blo = [&](int s) { return smem + s * Cfg::kStageBytes + 2 * Cfg::kABytes + Cfg::kBBytes; };
+  auto stage_blo = [&](int s) { return smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes; };
 
   // Tile coordinates, grouped along M for L2 reuse of B.
   const int num_m_tiles = (p.M + BM - 1) / BM;
@@ -119,7 +125,9 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   const int m0 = m_tile * BM;
   // Output column base. For SwiGLU forward a tile covers BN/2 hidden units.
   const int n0 = n_tile * (EPI == kEpiSwiGLU ? BN / 2 : BN);
-  const int num_k = (p.K + BK - 1) / BK;
+  const int total_k = (p.K + BK - 1) / BK;
+  const int kt_begin = blockIdx.y * p.k_tiles_per_split;
+  const int num_k = max(0, min(total_k, kt_begin + p.k_tiles_per_split) - kt_begin);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -155,7 +163,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
         const int s = kt % STAGES;
         const int use = kt / STAGES;
         if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
-        const int k0 = kt * BK;
+        const int k0 = (kt_begin + kt) * BK;
         mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
         if (A_MN) {
 #pragma unroll
@@ -204,7 +212,8 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one_sync()) {
-      constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
+      // 3xTF32 reads A from TMEM, which is always K-major (lane = row).
+      constexpr uint32_t idesc = idesc_tf32(BM, BN, PASSES == 3 ? false : A_MN, B_MN);
       bool issued_any = false;
       for (int kt = 0; kt < num_k; ++kt) {
         const int s = kt % STAGES;
@@ -235,11 +244,12 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
           };
           const uint32_t acc = (first_in_chunk && ks == 0) ? 0u : 1u;
           if (PASSES == 3) {
-            const uint32_t a_lo = smem_u32(stage_alo(s));
+            const uint32_t ta_hi = tmem_base + Cfg::kATmem + s * 2 * BK + ks * 8;
+            const uint32_t ta_lo = ta_hi + BK;
             const uint32_t b_lo = smem_u32(stage_blo(s));
-            mma_tf32_ss(d_tmem, desc_a(a_lo), desc_b(b_hi), idesc, acc);
-            mma_tf32_ss(d_tmem, desc_a(a_hi), desc_b(b_lo), idesc, 1u);
-            mma_tf32_ss(d_tmem, desc_a(a_hi), desc_b(b_hi), idesc, 1u);
+            mma_tf32_ts(d_tmem, ta_lo, desc_b(b_hi), idesc, acc);
+            mma_tf32_ts(d_tmem, ta_hi, desc_b(b_lo), idesc, 1u);
+            mma_tf32_ts(d_tmem, ta_hi, desc_b(b_hi), idesc, 1u);
           } else {
             mma_tf32_ss(d_tmem, desc_a(a_hi), desc_b(b_hi), idesc, acc);
           }
@@ -315,7 +325,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
         group(c, v);
         const int col0 = n0 + c * 32;
         if (row_ok && col0 < p.N) {
-          float* crow = p.c + static_cast<long long>(row) * p.ldc + col0;
+          float* crow = p.c + blockIdx.y * p.split_stride + static_cast<long long>(row) * p.ldc + col0;
           const float* rrow = p.r ? p.r + static_cast<long long>(row) * p.ldr + col0 : nullptr;
           if (col0 + 32 <= p.N) {
 #pragma unroll
@@ -388,28 +398,60 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     }
   } else if (PASSES == 3 && warp >= 6) {
     // ------------------------------------------------------------ converter
+    // Thread = one row of the A tile (its TMEM lane): read the row from the
+    // TMA landing buffer (undoing the swizzle), split it into tf32 hi / lo and
+    // store both into this stage's TMEM columns. B is split in shared memory:
+    // hi in place, lo beside it.
     const int ct = threadIdx.x - 192;  // 0..127
+    const int row = (warp % 4) * 32 + lane;
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>((warp % 4) * 32) << 16);
     for (int kt = 0; kt < num_k; ++kt) {
       const int s = kt % STAGES;
       const int use = kt / STAGES;
       if (!mbar_wait_warp(&full_bar[s], use & 1, p.status, kStatusTimeoutFull)) break;
-      // A and B hi/lo regions are each contiguous; swizzling only permutes
-      // positions, so an elementwise pass over the bytes is layout-agnostic.
-      float4* a = reinterpret_cast<float4*>(stage_a(s));
-      float4* alo = reinterpret_cast<float4*>(stage_alo(s));
-      constexpr int kA4 = BM * BK / 4;
+      const uint8_t* a = stage_a(s);
+      uint32_t hi[BK], lo[BK];
+      if (A_MN) {
+        // [row / 32][k][128 B], 32-byte granules XOR-swizzled by (k & 3).
+        const uint8_t* base = a + (row / 32) * 32 * BK * 4;
+        const int b = (row % 32) * 4;
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+          const int phys = (((b >> 5) ^ (k & 3)) << 5) | (b & 31);
+          const float x = *reinterpret_cast<const float*>(base + k * 128 + phys);
+          const float h = to_tf32(x);
+          hi[k] = __float_as_uint(h);
+          lo[k] = __float_as_uint(to_tf32(x - h));
+        }
+      } else {
+        // Row of 128 bytes, 16-byte chunks XOR-swizzled by (row & 7).
+#pragma unroll
+        for (int c = 0; c < BK / 4; ++c) {
+          const float4 x = *reinterpret_cast<const float4*>(a + row * 128 + ((c ^ (row & 7)) << 4));
+          const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float h = to_tf32(xs[e]);
+            hi[4 * c + e] = __float_as_uint(h);
+            lo[4 * c + e] = __float_as_uint(to_tf32(xs[e] - h));
+          }
+        }
+      }
+      tmem_st32(lane_addr + Cfg::kATmem + s * 2 * BK, hi);
+      tmem_st32(lane_addr + Cfg::kATmem + s * 2 * BK + BK, lo);
+      float4* bsrc = reinterpret_cast<float4*>(stage_b(s));
+      float4* bdst = reinterpret_cast<float4*>(stage_blo(s));
       constexpr int kB4 = BN * BK / 4;
 #pragma unroll 4
-      for (int i = ct; i < kA4 + kB4; i += 128) {
-        float4* src = i < kA4 ? a + i : reinterpret_cast<float4*>(stage_b(s)) + (i - kA4);
-        float4* dst = i < kA4 ? alo + i : reinterpret_cast<float4*>(stage_blo(s)) + (i - kA4);
-        float4 x = *src;
-        float4 hi = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
-        float4 lo = make_float4(to_tf32(x.x - hi.x), to_tf32(x.y - hi.y), to_tf32(x.z - hi.z), to_tf32(x.w - hi.w));
-        *src = hi;
-        *dst = lo;
+      for (int i = ct; i < kB4; i += 128) {
+        const float4 x = bsrc[i];
+        const float4 h = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
+        bsrc[i] = h;
+        bdst[i] = make_float4(to_tf32(x.x - h.x), to_tf32(x.y - h.y), to_tf32(x.z - h.z), to_tf32(x.w - h.w));
       }
+      tmem_st_wait();
       fence_proxy_async_smem();
+      tc_fence_before();
       mbar_arrive(&conv_bar[s]);
     }
   }

@@ -120,3 +120,27 @@ def test_linear_autograd_matches_fp64():
     (xd @ wd).backward(gy.double())
     assert _rel_err(x.grad, xd.grad) < 1e-5
     assert _rel_err(w.grad, wd.grad) < 1e-5
+
+
+@pytest.mark.parametrize("mode", ["tf32", "fp32"])
+def test_split_k_wgrad_shape_with_epilogue(mode):
+    # Few output tiles and a long K: runs as split-K with a deterministic reduce.
+    torch.manual_seed(6)
+    x = torch.randn(16384, 768, device="cuda")
+    dy = torch.randn(16384, 2048, device="cuda")
+    r = torch.randn(768, 2048, device="cuda")
+    c0 = torch.randn(768, 2048, device="cuda")
+    precision.set_precision(mode)
+    try:
+        out = c0.clone()
+        gemm.matmul(x, dy, trans_a=True, alpha=0.25, residual=r, out=out, accumulate=True)
+        again = c0.clone()
+        gemm.matmul(x, dy, trans_a=True, alpha=0.25, residual=r, out=again, accumulate=True)
+    finally:
+        precision.set_precision("fp32")
+    torch.cuda.synchronize()
+    check_status()
+    assert torch.equal(out, again)  # deterministic
+    ref = 0.25 * (x.double().t() @ dy.double()) + r.double() + c0.double()
+    tol = 2e-3 if mode == "tf32" else 2e-6
+    assert _rel_err(out, ref) < tol

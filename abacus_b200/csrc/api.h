@@ -49,3 +49,10 @@ void flash_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes);
 }  // namespace attn
 }  // namespace abacus
+
+namespace abacus {
+namespace comm {
+void wait_flag(torch::Tensor flag, int64_t expected, double timeout_ms, torch::Tensor result);
+void set_flag(torch::Tensor flag, int64_t value);
+}  // namespace comm
+}  // namespace abacus

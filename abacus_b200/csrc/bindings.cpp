@@ -19,6 +19,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_fwd", &abacus::attn::flash_attn_fwd);
   m.def("flash_attn_bwd", &abacus::attn::flash_attn_bwd);
   m.def("launch_count", &abacus::host::launch_count, "number of abacus kernels launched by this process");
+  m.def("wait_flag", &abacus::comm::wait_flag, "bounded device wait for a flag (error status on timeout)");
+  m.def("set_flag", &abacus::comm::set_flag, "release-store a device flag");
   m.def("read_status", &abacus::host::read_status, "device status word (0 = healthy)");
   m.def("reset_status", &abacus::host::reset_status, "clear the device status word");
 }

@@ -167,11 +167,10 @@ def _grouped_experts(x_TD, weights_TK, indices_TK, w_gate_EDM, w_up_EDM, w_down_
     outs = []
     start = 0
     for e, n in enumerate(counts):
-        if n > 0:
-            outs.append(_expert_forward(xs[start : start + n], w_gate_EDM[e], w_up_EDM[e], w_down_EMD[e]))
+        # Empty slabs still run, so an idle expert gets a zero gradient rather
+        # than none (expert-parallel ranks compare shard by shard).
+        outs.append(_expert_forward(xs[start : start + n], w_gate_EDM[e], w_up_EDM[e], w_down_EMD[e]))
         start += n
-    if not outs:
-        return x_TD.new_zeros(x_TD.shape)
     y = torch.cat(outs, dim=0) * w_sorted.unsqueeze(-1)
     return x_TD.new_zeros(x_TD.shape).index_add(0, token_of, y)
 
@@ -329,13 +328,8 @@ class MoEExpertParallel(torch.nn.Module):
         payload = torch.cat([repeated_SD[order], send_ids], dim=-1)
         received = _AllToAll.apply(payload, input_splits, output_splits, "ep")
         recv_SD, recv_ids = received[:, :-1], received[:, -1].detach().round().long() - self.expert_offset
-        if recv_SD.shape[0] > 0:
-            ones = torch.ones(recv_SD.shape[0], 1, device=recv_SD.device, dtype=recv_SD.dtype)
-            expert_SD = _grouped_experts(
-                recv_SD, ones, recv_ids.unsqueeze(-1), self.w_gate_EDM, self.w_up_EDM, self.w_down_EMD
-            )
-        else:
-            expert_SD = recv_SD * 0
+        ones = torch.ones(recv_SD.shape[0], 1, device=recv_SD.device, dtype=recv_SD.dtype)
+        expert_SD = _grouped_experts(recv_SD, ones, recv_ids.unsqueeze(-1), self.w_gate_EDM, self.w_up_EDM, self.w_down_EMD)
         returned_SD = _AllToAll.apply(expert_SD, output_splits, input_splits, "ep")
         inverse = torch.empty_like(order)
         inverse[order] = torch.arange(order.shape[0], device=order.device)

@@ -87,7 +87,15 @@ class _Bucket:
 class DataParallel:
     """Replica of one model per rank. Gradients are the mean over every rank's tokens."""
 
-    def __init__(self, model: torch.nn.Module, stage: int = 0, bucket_mb: float = 25.0, exclude=None, dim: str = DIM):
+    def __init__(
+        self,
+        model: torch.nn.Module,
+        stage: int = 0,
+        bucket_mb: float = 25.0,
+        exclude=None,
+        dim: str = DIM,
+        token_weighted: bool = True,
+    ):
         if not dist.is_initialized():
             raise RuntimeError("Call init_process_group before DataParallel")
         if stage not in (0, 1, 2, 3):
@@ -100,6 +108,12 @@ class DataParallel:
         self.src = mesh.global_rank(dim, 0)
         self.bucket_bytes = int(bucket_mb * 1024 * 1024)
         self.excluded = {id(p) for p in (exclude or [])}
+        # token_weighted: each rank's loss is its local mean, gradients are
+        # combined as sum(count_r * g_r) / sum(count_r) (the reference).
+        # Otherwise each rank's loss is already divided by the global count and
+        # gradients are plain sums (used when expert weights receive every
+        # rank's tokens through the expert-parallel all-to-all).
+        self.token_weighted = token_weighted
         self.partitions: list[_Partition] = []
         self.owned: dict[int, tuple[int, int]] | None = None
         self.grad_shards: dict[int, torch.Tensor] | None = None
@@ -186,6 +200,10 @@ class DataParallel:
 
     # ------------------------------------------------------------------ loss
     def _mean_loss(self, loss, token_count):
+        if not self.token_weighted:
+            packed = loss.detach().reshape(1).clone()
+            self._all_reduce(packed)
+            return packed[0], torch.ones((), dtype=loss.dtype, device=loss.device)
         count = torch.as_tensor(token_count, dtype=loss.dtype, device=loss.device).reshape(())
         packed = torch.stack((loss.detach().reshape(()) * count, count))
         self._all_reduce(packed)
@@ -228,8 +246,11 @@ class DataParallel:
         bucket.ready.add(pi)
         self._launch_ready()
 
+    def _multiplier(self):
+        return self._token_count if self.token_weighted else 1.0
+
     def _launch(self, bucket):
-        count = self._token_count
+        count = self._multiplier()
         if isinstance(count, torch.Tensor):
             bucket.flat.mul_(count.to(bucket.flat.dtype))
         else:
@@ -275,7 +296,7 @@ class DataParallel:
             if p.grad is None:
                 raise RuntimeError("backward produced no gradient for a parameter")
             flat[off : off + n].copy_(p.grad.reshape(-1))
-        flat.mul_(torch.as_tensor(token_count, dtype=flat.dtype, device=flat.device))
+        flat.mul_(torch.as_tensor(token_count if self.token_weighted else 1.0, dtype=flat.dtype, device=flat.device))
         return flat
 
     def _all_reduce_grads(self, token_count, total):
@@ -398,7 +419,7 @@ class DataParallel:
         flat = torch.zeros(part.padded, dtype=p.dtype, device=p.device)
         for q, off, n in zip(part.params, part.offsets, part.numels):
             flat[off : off + n].copy_(part.pending[id(q)].reshape(-1))
-        flat.mul_(torch.as_tensor(self._token_count, dtype=flat.dtype, device=flat.device))
+        flat.mul_(torch.as_tensor(self._multiplier(), dtype=flat.dtype, device=flat.device))
         self._scatter_owned_grads(part, flat, None)
         part.pending.clear()
         self._reshard(part)

@@ -102,7 +102,12 @@ class Trainer:
         token_count = (targets != IGNORE).sum()
         if not tokens_BL.is_cuda and int(token_count) < 1:
             raise ValueError("batch has no target tokens")
-        loss = self.model(inputs_BL, targets=targets, normalizer=token_count.to(torch.float32))
+        normalizer = token_count.to(torch.float32)
+        if self.parallel is not None and not self.parallel.token_weighted:
+            # Loss divided by the global token count; gradients are then summed.
+            normalizer = normalizer.clone()
+            dist.all_reduce(normalizer, op=dist.ReduceOp.SUM, group=self.parallel.group)
+        loss = self.model(inputs_BL, targets=targets, normalizer=normalizer)
         loss = self._with_aux_loss(loss)
         self.optimizer.zero_grad()
         if self.print_memory:

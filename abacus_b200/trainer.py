@@ -91,8 +91,11 @@ class Trainer:
         if self.pipeline is not None:
             self.optimizer.zero_grad()
             loss = self.pipeline.forward_backward(tokens_BL).detach()
-            if getattr(self.model, "context_parallel", False):
+            if getattr(self.model, "context_parallel", False) and mesh.rank_and_world_size("cp")[1] > 1:
                 sum_parameter_gradients(self.model)
+                # Each CP rank of the last stage holds its shard's share of the loss.
+                loss = loss.clone()
+                dist.all_reduce(loss, op=dist.ReduceOp.SUM, group=mesh.group_for("cp"))
             self._optimizer_step()
             return loss, loss
         inputs_BL = tokens_BL.clamp(min=0)  # -100 is padding; the embedding has no row for it

@@ -54,5 +54,10 @@ namespace abacus {
 namespace comm {
 void wait_flag(torch::Tensor flag, int64_t expected, double timeout_ms, torch::Tensor result);
 void set_flag(torch::Tensor flag, int64_t value);
+void symm_barrier(std::vector<int64_t> signal_ptrs, int64_t rank, int64_t slot_base, int64_t epoch, double timeout_ms,
+                  std::vector<int64_t> exch_ptrs, c10::optional<torch::Tensor> payload);
+void ar_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, torch::Tensor counts, bool normalize,
+              int64_t rank, int64_t lo, int64_t hi, torch::Tensor exp_avg, torch::Tensor exp_avg_sq, double lr,
+              double beta1, double beta2, double eps, double weight_decay, int64_t step);
 }  // namespace comm
 }  // namespace abacus

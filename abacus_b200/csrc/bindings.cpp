@@ -21,6 +21,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", &abacus::host::launch_count, "number of abacus kernels launched by this process");
   m.def("wait_flag", &abacus::comm::wait_flag, "bounded device wait for a flag (error status on timeout)");
   m.def("set_flag", &abacus::comm::set_flag, "release-store a device flag");
+  m.def("symm_barrier", &abacus::comm::symm_barrier, "bounded system-scope barrier over peer signal pads");
+  m.def("ar_adamw", &abacus::comm::ar_adamw, "peer-memory gradient reduce + AdamW + parameter broadcast");
   m.def("read_status", &abacus::host::read_status, "device status word (0 = healthy)");
   m.def("reset_status", &abacus::host::reset_status, "clear the device status word");
+  m.def(
+      "status_tensor",
+      [](int64_t device) {
+        // A one-element int32 view of the status word, for asynchronous reads.
+        return torch::from_blob(abacus::host::status_ptr(static_cast<int>(device)), {1},
+                                torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, device));
+      },
+      "device status word as a 1-element CUDA tensor (no copy)");
 }

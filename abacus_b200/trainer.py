@@ -80,6 +80,9 @@ class Trainer:
             self.model, lr=1e-3 if lr is None else lr, betas=betas, eps=eps, weight_decay=weight_decay,
             owned=owned, grad_shards=grad_shards,
         )
+        self._fused = bool(getattr(parallel, "fused_optimizer", False))
+        if self._fused:
+            parallel.bind_optimizer(self.optimizer)
         self.scheduler = WSD(total_steps, lr=schedule_lr) if total_steps is not None else None
         if self.scheduler is not None:
             self.optimizer.lr = self.scheduler.learning_rate(1)
@@ -137,7 +140,11 @@ class Trainer:
     def _optimizer_step(self) -> None:
         if self.scheduler is not None:
             self.optimizer.lr = self.scheduler.step()
-        self.optimizer.step()
+        if self._fused:
+            # Gradient reduction, AdamW and the parameter broadcast in one kernel.
+            self.parallel.step_optimizer(self.optimizer)
+        else:
+            self.optimizer.step()
 
     def _context_parallel_active(self) -> bool:
         if not getattr(self.model, "context_parallel", False):

@@ -55,6 +55,8 @@ def parse_args():
     p.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
     p.add_argument("--seq-len", type=int, default=SEQ_LEN)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--dp", choices=("fused", "nccl"), default="fused",
+                   help="N>1: fused peer-memory reduce+AdamW kernel, or NCCL bucketed all-reduce + AdamW")
     return p.parse_args()
 
 
@@ -160,14 +162,17 @@ def timed_steps(step_fn, batches, steps, world, device):
 def build_abacus(args, world, device):
     sys.path.insert(0, ROOT)
     from abacus_b200.ops import precision
-    from abacus_b200.distributed.data_parallel import DataParallel
+    from abacus_b200.distributed.data_parallel import DataParallel, FusedDataParallel
     from abacus_b200.trainer import Trainer
     from abacus_b200.transformer import Transformer
 
     precision.set_precision(args.precision)
     torch.manual_seed(0)
     model = Transformer(**MODEL, hidden_dim=HIDDEN)
-    parallel = DataParallel(model.to(device), stage=0) if world > 1 else None
+    parallel = None
+    if world > 1:
+        model = model.to(device)
+        parallel = FusedDataParallel(model) if args.dp == "fused" else DataParallel(model, stage=0)
     trainer = Trainer(model, parallel, total_steps=args.warmup + 2 * args.steps + 2)
     return trainer
 
@@ -278,6 +283,9 @@ def main():
                 "global_batch": args.global_batch,
                 "seq_len": args.seq_len,
                 "parallelism": f"dp{world}" if world > 1 else "single",
+                "dp_comm": None if world == 1 else (
+                    "fused NVLink peer-memory gradient reduce + AdamW + broadcast kernel"
+                    if impl == "abacus" and args.dp == "fused" else "NCCL all-reduce, then AdamW"),
                 "l2": "inputs/activations larger than L2 (no flush needed)",
                 "compute": "3xTF32 split precision on tcgen05 (fp32 accuracy)" if args.precision == "fp32" and impl == "abacus"
                 else ("tf32 tcgen05" if impl == "abacus" else "reference: torch fp32 (TF32 off)"),
@@ -290,6 +298,13 @@ def main():
             line["impl"] = "reference"
         print(json.dumps(line), flush=True)
     if world > 1:
+        parallel = getattr(trainer, "parallel", None)
+        if hasattr(parallel, "check"):
+            parallel.check()
+        torch.cuda.synchronize()
+        dist.barrier()
+        if hasattr(parallel, "release"):
+            parallel.release()
         dist.destroy_process_group()
 
 

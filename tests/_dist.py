@@ -14,7 +14,7 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def _entry(rank, world, port, fn, args, timeout_s):
+def _entry(rank, world, port, fn, args, timeout_s, backend="gloo"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["RANK"] = str(rank)
@@ -24,7 +24,13 @@ def _entry(rank, world, port, fn, args, timeout_s):
     from abacus_b200.parallel import mesh
     from abacus_b200.utils.dist import init_process_group
 
-    init_process_group("gloo", timeout_s=timeout_s)
+    device = None
+    if backend == "nccl":
+        import torch
+
+        torch.cuda.set_device(rank)
+        device = torch.device("cuda", rank)
+    init_process_group(backend, device=device, timeout_s=timeout_s)
     try:
         fn(rank, world, *args)
     except Exception:
@@ -35,6 +41,7 @@ def _entry(rank, world, port, fn, args, timeout_s):
         dist.destroy_process_group()
 
 
-def run_ranks(fn, world: int, *args, timeout_s: float = 120.0):
-    """Run fn(rank, world, *args) on `world` gloo ranks; fails if any rank fails."""
-    mp.spawn(_entry, args=(world, free_port(), fn, args, timeout_s), nprocs=world, join=True)
+def run_ranks(fn, world: int, *args, timeout_s: float = 120.0, backend: str = "gloo"):
+    """Run fn(rank, world, *args) on `world` ranks (gloo on CPU, or nccl with
+    rank r on cuda:r); fails if any rank fails."""
+    mp.spawn(_entry, args=(world, free_port(), fn, args, timeout_s, backend), nprocs=world, join=True)

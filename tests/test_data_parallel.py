@@ -74,3 +74,17 @@ def _dp_owned(rank, world):
 
 def test_owned_slices_partition_every_parameter():
     run_ranks(_dp_owned, 2)
+
+
+def _fused_needs_cuda(rank, world):
+    import pytest
+
+    from abacus_b200.distributed.data_parallel import FusedDataParallel
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        model = _make()
+        Trainer(model, FusedDataParallel(model), device="cpu")
+
+
+def test_fused_data_parallel_rejects_cpu_parameters():
+    run_ranks(_fused_needs_cuda, 2)

@@ -7,6 +7,8 @@ namespace abacus {
 namespace gemm {
 void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
               int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate, int64_t passes);
+void gemm_batched(torch::Tensor c, torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, double alpha,
+                  int64_t causal, int64_t passes);
 void gemm_swiglu(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
                  torch::Tensor h, int64_t passes);
 void gemm_swiglu_bwd(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u, torch::Tensor dgu,
@@ -40,6 +42,8 @@ void adamw_step(std::vector<torch::Tensor> params, std::vector<torch::Tensor> gr
 
 namespace abacus {
 namespace attn {
+void causal_softmax_fwd(torch::Tensor s);
+void causal_softmax_bwd(torch::Tensor p, torch::Tensor dp, double scale);
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                     int64_t batch, int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes);

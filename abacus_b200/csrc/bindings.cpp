@@ -5,6 +5,7 @@
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_out", &abacus::gemm::gemm_out, "tcgen05 tf32 / 3xTF32 GEMM into C");
+  m.def("gemm_batched", &abacus::gemm::gemm_batched, "batched tcgen05 GEMM over (B, H, rows, cols) views");
   m.def("gemm_swiglu", &abacus::gemm::gemm_swiglu, "gate/up GEMM with SwiGLU epilogue");
   m.def("gemm_swiglu_bwd", &abacus::gemm::gemm_swiglu_bwd, "down-projection dgrad with SwiGLU backward epilogue");
   m.def("rmsnorm_fwd", &abacus::ops::rmsnorm_fwd);
@@ -16,6 +17,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_fwd_bwd", &abacus::ops::cross_entropy_fwd_bwd);
   m.def("cross_entropy_grad", &abacus::ops::cross_entropy_grad);
   m.def("adamw_step", &abacus::ops::adamw_step);
+  m.def("causal_softmax_fwd", &abacus::attn::causal_softmax_fwd, "in-place causal row softmax (materialised attention)");
+  m.def("causal_softmax_bwd", &abacus::attn::causal_softmax_bwd, "in-place dS from P and dP (materialised attention)");
   m.def("flash_attn_fwd", &abacus::attn::flash_attn_fwd);
   m.def("flash_attn_bwd", &abacus::attn::flash_attn_bwd);
   m.def("launch_count", &abacus::host::launch_count, "number of abacus kernels launched by this process");

@@ -202,6 +202,84 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
   abacus::host::note_launch();
 }
 
+namespace {
+
+// 4-D fp32 tensor map over a (B, H, rows, inner) strided view.
+CUtensorMap make_map4(const torch::Tensor& t, int box_inner, int box_rows, bool mn_major) {
+  CUtensorMap m;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(t.size(3)), static_cast<cuuint64_t>(t.size(2)),
+                        static_cast<cuuint64_t>(t.size(1)), static_cast<cuuint64_t>(t.size(0))};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.stride(2) * 4), static_cast<cuuint64_t>(t.stride(1) * 4),
+                           static_cast<cuuint64_t>(t.stride(0) * 4)};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapSwizzle sw = mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  CUresult r = host::encode_tiled()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, t.data_ptr(), dims, strides, box, estr,
+                                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (4-D) failed with code ", static_cast<int>(r));
+  return m;
+}
+
+void check_batched(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32 && t.dim() == 4, name,
+              " must be a 4-D (B, H, rows, cols) CUDA fp32 view");
+  TORCH_CHECK(t.stride(3) == 1, name, " must have unit inner stride");
+  for (int d = 0; d < 3; ++d)
+    TORCH_CHECK(t.stride(d) % 4 == 0, name, " strides must be multiples of 4 elements (16 bytes) for TMA");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned for TMA");
+}
+
+}  // namespace
+
+// Batched C[b, h] = alpha * op(A[b, h]) @ op(B[b, h]) over (B, H, rows, cols)
+// strided views (heads of a packed projection need no copy). `causal` selects
+// the attention-shaped tile skipping described in gemm_tcgen05.cuh.
+void gemm_batched(torch::Tensor c, torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, double alpha,
+                  int64_t causal, int64_t passes) {
+  check_passes(passes);
+  const c10::cuda::CUDAGuard guard(a.device());
+  check_batched(a, "A");
+  check_batched(b, "B");
+  check_batched(c, "C");
+  TORCH_CHECK(a.size(0) == b.size(0) && a.size(1) == b.size(1) && c.size(0) == a.size(0) && c.size(1) == a.size(1),
+              "batch dimensions differ");
+  const bool a_mn = trans_a, b_mn = !trans_b;
+  const int64_t M = a_mn ? a.size(3) : a.size(2), K = a_mn ? a.size(2) : a.size(3);
+  const int64_t N = b_mn ? b.size(3) : b.size(2), Kb = b_mn ? b.size(2) : b.size(3);
+  TORCH_CHECK(K == Kb, "inner dimensions differ: ", K, " vs ", Kb);
+  TORCH_CHECK(c.size(2) == M && c.size(3) == N, "C shape mismatch");
+  TORCH_CHECK(causal >= 0 && causal <= 3, "causal mode must be 0..3");
+  TORCH_CHECK(causal == 0 || (M == K || causal == 1), "causal modes 2/3 need a square (queries x keys) operand");
+  const int64_t Z = a.size(0) * a.size(1);
+  if (M == 0 || N == 0 || Z == 0) return;
+  TORCH_CHECK(K > 0, "empty inner dimension");
+  TORCH_CHECK(Z <= 65535, "at most 65535 matrices per batched GEMM");
+  const int BN = pick_bn(N, static_cast<int>(passes));
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.tma_a = a_mn ? make_map4(a, 32, BK, true) : make_map4(a, BK, BM, false);
+  p.tma_b[0] = b_mn ? make_map4(b, 32, BK, true) : make_map4(b, BK, BN, false);
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.b_mode = kBSingle;
+  p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
+  p.alpha = static_cast<float>(alpha);
+  p.c = c.data_ptr<float>();
+  p.ldc = c.stride(2);
+  p.batched = 1;
+  p.batch_h = static_cast<int>(a.size(1));
+  p.c_stride_h = c.stride(1);
+  p.c_stride_b = c.stride(0);
+  p.causal = static_cast<int>(causal);
+  p.status = host::status_ptr(a.device().index());
+  p.k_tiles_per_split = static_cast<int>((K + BK - 1) / BK);
+  const long long tiles = ((M + BM - 1) / BM) * p.num_n_tiles;
+  launch_store(p, dim3(static_cast<unsigned>(tiles), 1, static_cast<unsigned>(Z)), BN, a_mn, b_mn,
+               static_cast<int>(passes), at::cuda::getCurrentCUDAStream());
+}
+
 // SwiGLU up-projection: g = x @ w_gate, u = x @ w_up, h = silu(g) * u.
 // x (T, D), w_gate / w_up (D, Mh) in the (in, out) layout.
 void gemm_swiglu(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,

@@ -59,6 +59,16 @@ struct alignas(64) Params {
   long long ld_gu;
   float* dgu;
   long long ld_dgu;
+  // Batched mode: every operand map is 4-D (inner, rows, H, B); blockIdx.z =
+  // b * batch_h + h selects the matrix, C is offset by b*c_stride_b + h*c_stride_h.
+  int batched;
+  int batch_h;
+  long long c_stride_h, c_stride_b;
+  // Causal structure of attention-shaped products (square, queries = keys):
+  //   1: skip tiles strictly above the diagonal (n0 >= m0 + BM), C untouched
+  //   2: K range [0, m0 + BM)   (P @ V, dS @ K: keys after the last query)
+  //   3: K range [m0, K)        (dS^T @ Q, P^T @ dO: queries before the first key)
+  int causal;
   int* status;
 };
 
@@ -125,9 +135,19 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   const int m0 = m_tile * BM;
   // Output column base. For SwiGLU forward a tile covers BN/2 hidden units.
   const int n0 = n_tile * (EPI == kEpiSwiGLU ? BN / 2 : BN);
-  const int total_k = (p.K + BK - 1) / BK;
-  const int kt_begin = blockIdx.y * p.k_tiles_per_split;
+  if (p.causal == 1 && n0 >= m0 + BM) return;  // fully masked tile (uniform exit)
+  int total_k = (p.K + BK - 1) / BK;
+  int kt_first = 0;
+  if (p.causal == 2) total_k = min(total_k, (m0 + BM + BK - 1) / BK);
+  if (p.causal == 3) kt_first = m0 / BK;
+  const int kt_begin = kt_first + blockIdx.y * p.k_tiles_per_split;
   const int num_k = max(0, min(total_k, kt_begin + p.k_tiles_per_split) - kt_begin);
+  const int bz_h = p.batched ? static_cast<int>(blockIdx.z) % p.batch_h : 0;
+  const int bz_b = p.batched ? static_cast<int>(blockIdx.z) / p.batch_h : 0;
+  auto load = [&](void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    if (p.batched) tma_load_4d(dst, map, bar, x, y, bz_h, bz_b);
+    else tma_load_2d(dst, map, bar, x, y);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -167,9 +187,9 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
         mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
         if (A_MN) {
 #pragma unroll
-          for (int c = 0; c < BM / 32; ++c) tma_load_2d(stage_a(s) + c * 32 * BK * 4, &p.tma_a, &full_bar[s], m0 + 32 * c, k0);
+          for (int c = 0; c < BM / 32; ++c) load(stage_a(s) + c * 32 * BK * 4, &p.tma_a, &full_bar[s], m0 + 32 * c, k0);
         } else {
-          tma_load_2d(stage_a(s), &p.tma_a, &full_bar[s], k0, m0);
+          load(stage_a(s), &p.tma_a, &full_bar[s], k0, m0);
         }
         // B source for this (n, k) tile.
         const CUtensorMap* bmap = &p.tma_b[0];
@@ -187,19 +207,19 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
           if (p.b_mode == kBDualN) {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c) {
-              tma_load_2d(stage_b(s) + c * 32 * BK * 4, &p.tma_b[0], &full_bar[s], n0 + 32 * c, k0);
-              tma_load_2d(stage_b(s) + (c + BN / 64) * 32 * BK * 4, &p.tma_b[1], &full_bar[s], n0 + 32 * c, k0);
+              load(stage_b(s) + c * 32 * BK * 4, &p.tma_b[0], &full_bar[s], n0 + 32 * c, k0);
+              load(stage_b(s) + (c + BN / 64) * 32 * BK * 4, &p.tma_b[1], &full_bar[s], n0 + 32 * c, k0);
             }
           } else {
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c) tma_load_2d(stage_b(s) + c * 32 * BK * 4, bmap, &full_bar[s], bn + 32 * c, bk);
+            for (int c = 0; c < BN / 32; ++c) load(stage_b(s) + c * 32 * BK * 4, bmap, &full_bar[s], bn + 32 * c, bk);
           }
         } else {
           if (p.b_mode == kBDualN) {
-            tma_load_2d(stage_b(s), &p.tma_b[0], &full_bar[s], k0, n0);
-            tma_load_2d(stage_b(s) + (BN / 2) * BK * 4, &p.tma_b[1], &full_bar[s], k0, n0);
+            load(stage_b(s), &p.tma_b[0], &full_bar[s], k0, n0);
+            load(stage_b(s) + (BN / 2) * BK * 4, &p.tma_b[1], &full_bar[s], k0, n0);
           } else {
-            tma_load_2d(stage_b(s), bmap, &full_bar[s], bk, bn);
+            load(stage_b(s), bmap, &full_bar[s], bk, bn);
           }
         }
         ++issued;
@@ -325,7 +345,8 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
         group(c, v);
         const int col0 = n0 + c * 32;
         if (row_ok && col0 < p.N) {
-          float* crow = p.c + blockIdx.y * p.split_stride + static_cast<long long>(row) * p.ldc + col0;
+          float* crow = p.c + blockIdx.y * p.split_stride + bz_b * p.c_stride_b + bz_h * p.c_stride_h +
+                        static_cast<long long>(row) * p.ldc + col0;
           const float* rrow = p.r ? p.r + static_cast<long long>(row) * p.ldr + col0 : nullptr;
           if (col0 + 32 <= p.N) {
 #pragma unroll

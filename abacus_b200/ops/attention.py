@@ -140,6 +140,61 @@ class _Flash(torch.autograd.Function):
         return dq, dk, dv, None, None, None, None, None
 
 
+class _DenseCausal(torch.autograd.Function):
+    """Materialised causal attention on the batched tcgen05 GEMM: S = scale QK^T
+    (tiles above the diagonal skipped), in-place softmax, O = P V; backward
+    dP = dO V^T, dS = P (dP - rowsum(P dP)) scale, dQ = dS K, dK = dS^T Q,
+    dV = P^T dO. Used for head dims the fp32-accurate flash tiles do not cover
+    (the reference's own formulation, ``abacus/attention.py:175-213``)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, batch, heads, head_dim):
+        t = q.shape[0]
+        length = t // batch
+        scale = 1.0 / math.sqrt(head_dim)
+        passes = precision.passes()
+
+        def heads_view(x):
+            return x.view(batch, length, heads, head_dim).permute(0, 2, 1, 3)
+
+        s = torch.empty(batch, heads, length, length, device=q.device, dtype=torch.float32)
+        ext().gemm_batched(s, heads_view(q), heads_view(k), False, True, scale, 1, passes)
+        ext().causal_softmax_fwd(s)
+        out = torch.empty(t, heads * head_dim, device=q.device, dtype=torch.float32)
+        ext().gemm_batched(heads_view(out), s, heads_view(v), False, False, 1.0, 2, passes)
+        ctx.save_for_backward(q, k, v, s)
+        ctx.dims = (batch, heads, head_dim, length, scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        q, k, v, p = ctx.saved_tensors
+        batch, heads, head_dim, length, scale = ctx.dims
+        passes = precision.passes()
+
+        def heads_view(x):
+            return x.view(batch, length, heads, head_dim).permute(0, 2, 1, 3)
+
+        do = heads_view(grad_out.contiguous())
+        dp = torch.empty_like(p)
+        ext().gemm_batched(dp, do, heads_view(v), False, True, 1.0, 1, passes)
+        ext().causal_softmax_bwd(p, dp, scale)
+        dq = torch.empty(q.shape[0], heads * head_dim, device=q.device, dtype=torch.float32)
+        dk = torch.empty_like(dq)
+        dv = torch.empty_like(dq)
+        ext().gemm_batched(heads_view(dq), dp, heads_view(k), False, False, 1.0, 2, passes)
+        ext().gemm_batched(heads_view(dk), dp, heads_view(q), True, False, 1.0, 3, passes)
+        ext().gemm_batched(heads_view(dv), p, do, True, False, 1.0, 3, passes)
+        return dq, dk, dv, None, None, None
+
+
+def _flash_supports(head_dim: int) -> bool:
+    """Head dims the flash kernels cover in the current precision mode."""
+    if precision.passes() == 3:
+        return head_dim in (32, 64)
+    return head_dim in (32, 64, 128)
+
+
 _TABLES: dict = {}
 
 
@@ -163,7 +218,14 @@ def qk_prologue(qkv, heads, head_dim, q_gamma, k_gamma, inv_freq, seq_len, posit
 
 def flash_attention(q, k, v, batch, heads, head_dim, q_pos=None, k_pos=None):
     """CUDA flash attention over (T, HK) token-major tensors. Without positions
-    the mask is plain causal over each sequence (requires Lq == Lk)."""
+    the mask is plain causal over each sequence (requires Lq == Lk). Head dims
+    without an fp32-accurate flash tile (128 in fp32 mode) take the
+    materialised path for plain causal masks."""
+    if not _flash_supports(head_dim):
+        if q_pos is not None or k_pos is not None or q.shape[0] != k.shape[0]:
+            raise NotImplementedError(
+                f"head_dim {head_dim} in fp32 mode supports plain causal attention only (no positions)")
+        return _DenseCausal.apply(q, k, v, batch, heads, head_dim)
     return _Flash.apply(q, k, v, q_pos, k_pos, batch, heads, head_dim)
 
 

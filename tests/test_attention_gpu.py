@@ -130,3 +130,27 @@ def test_flash_backward_with_zigzag_positions(mode):
     assert _err(q.grad.cpu(), dq_ref) < tol
     assert _err(k.grad.cpu(), dk_ref) < tol
     assert _err(v.grad.cpu(), dv_ref) < tol
+
+
+@pytest.mark.parametrize("batch,length,heads", [(1, 256, 1), (2, 384, 2), (1, 200, 2)])
+def test_dense_head_dim_128_fp32_forward_backward(batch, length, heads):
+    """head_dim 128 in fp32 mode: materialised attention on the batched GEMM
+    (causal tile skipping) + the in-place softmax kernels, against fp64."""
+    torch.manual_seed(3)
+    hd = 128
+    t = batch * length
+    q = torch.randn(t, heads * hd, device="cuda", requires_grad=True)
+    k = torch.randn(t, heads * hd, device="cuda", requires_grad=True)
+    qkv = torch.randn(t, 3 * heads * hd, device="cuda")
+    v = qkv[:, 2 * heads * hd :].clone().requires_grad_()
+    gout = torch.randn(t, heads * hd, device="cuda")
+    precision.set_precision("fp32")
+    out = attn_ops.flash_attention(q, k, v, batch, heads, hd)
+    out.backward(gout)
+    torch.cuda.synchronize()
+    check_status()
+    pos = torch.arange(length)
+    ref_o, rq, rk, rv = _ref_grads(q, k, v, batch, heads, hd, pos, pos, gout)
+    assert _err(out.detach().cpu(), ref_o) < 2e-5
+    for got, want in ((q.grad, rq), (k.grad, rk), (v.grad, rv)):
+        assert _err(got.cpu(), want) < 5e-5

@@ -144,3 +144,31 @@ def test_split_k_wgrad_shape_with_epilogue(mode):
     ref = 0.25 * (x.double().t() @ dy.double()) + r.double() + c0.double()
     tol = 2e-3 if mode == "tf32" else 2e-6
     assert _rel_err(out, ref) < tol
+
+
+@pytest.mark.parametrize("mode", ["tf32", "fp32"])
+@pytest.mark.parametrize("trans_a,trans_b", [(False, True), (False, False), (True, False)])
+def test_batched_gemm_strided_heads(mode, trans_a, trans_b):
+    """(B, H, rows, cols) strided views (heads of a packed projection)."""
+    from abacus_b200.ops._ext import check_status, ext
+
+    torch.manual_seed(5)
+    b, h, m, n, k = 2, 3, 192, 160, 96
+    def packed(rows, cols):
+        base = torch.randn(b, rows, h, cols + 4, device="cuda")[..., :cols]  # padded row stride
+        return base.permute(0, 2, 1, 3)
+    a = packed(k, m) if trans_a else packed(m, k)
+    bb = packed(n, k) if trans_b else packed(k, n)
+    c = torch.empty(b, h, m, n, device="cuda")
+    precision.set_precision(mode)
+    try:
+        ext().gemm_batched(c, a, bb, trans_a, trans_b, 0.5, 0, precision.passes())
+    finally:
+        precision.set_precision("fp32")
+    torch.cuda.synchronize()
+    check_status()
+    aa = a.double().transpose(-1, -2) if trans_a else a.double()
+    bm = bb.double().transpose(-1, -2) if trans_b else bb.double()
+    ref = 0.5 * aa @ bm
+    err = ((c.double() - ref).abs().max() / ref.abs().max()).item()
+    assert err < (3e-3 if mode == "tf32" else 2e-6)

@@ -7,6 +7,13 @@ namespace abacus {
 namespace gemm {
 void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
               int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate, int64_t passes);
+int64_t gemm_out_tp(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
+                    int64_t b_mode, double alpha, int64_t passes, c10::optional<std::vector<int64_t>> wait,
+                    c10::optional<std::vector<int64_t>> scatter);
+void gemm_swiglu_tp(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
+                    torch::Tensor h, int64_t passes, std::vector<int64_t> wait);
+void gemm_swiglu_bwd_tp(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u, torch::Tensor dgu,
+                        int64_t passes, std::vector<int64_t> wait);
 void gemm_batched(torch::Tensor c, torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, double alpha,
                   int64_t causal, int64_t passes);
 void gemm_swiglu(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
@@ -60,6 +67,10 @@ void wait_flag(torch::Tensor flag, int64_t expected, double timeout_ms, torch::T
 void set_flag(torch::Tensor flag, int64_t value);
 void symm_barrier(std::vector<int64_t> signal_ptrs, int64_t rank, int64_t slot_base, int64_t epoch, double timeout_ms,
                   std::vector<int64_t> exch_ptrs, c10::optional<torch::Tensor> payload);
+void tp_push_rows(torch::Tensor x, std::vector<int64_t> dst_ptrs, std::vector<int64_t> flag_ptrs, int64_t chunk,
+                  int64_t seq, int64_t self, int64_t epoch, torch::Tensor done);
+void tp_reduce_rows(torch::Tensor staging, int64_t world, torch::Tensor counters, int64_t target,
+                    c10::optional<torch::Tensor> residual, torch::Tensor out);
 void ar_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, torch::Tensor counts, bool normalize,
               int64_t rank, int64_t lo, int64_t hi, torch::Tensor exp_avg, torch::Tensor exp_avg_sq, double lr,
               double beta1, double beta2, double eps, double weight_decay, int64_t step);

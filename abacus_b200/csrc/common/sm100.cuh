@@ -16,6 +16,11 @@
 #ifndef ABACUS_WAIT_NS
 #define ABACUS_WAIT_NS 2000000000ull  // 2 s per wait
 #endif
+// Waits on another GPU's progress (its kernels may legitimately run a whole
+// layer behind) use a longer bound.
+#ifndef ABACUS_PEER_WAIT_NS
+#define ABACUS_PEER_WAIT_NS 30000000000ull  // 30 s
+#endif
 
 namespace abacus {
 
@@ -108,6 +113,40 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code) {
   const bool ok = mbar_wait(bar, parity, status, code);
   return __all_sync(0xffffffffu, ok);
+}
+
+// ---------------------------------------------------------------- peer flags
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *flag >= target (signed compare of monotonic counters
+// that another GPU advances). On timeout records kStatusTimeoutPeer.
+__device__ __forceinline__ bool wait_flag_geq(const int* flag, int target, int* status) {
+  if (ld_acquire_sys(flag) - target >= 0) return true;
+  const uint64_t start = globaltimer_ns();
+  uint32_t iter = 0;
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_sys(flag) - target >= 0) return true;
+    if ((++iter & 63u) == 0) {
+      if (status != nullptr && *reinterpret_cast<volatile int*>(status) != kStatusOk) return false;
+      if (globaltimer_ns() - start > ABACUS_PEER_WAIT_NS) {
+        if (status != nullptr) atomicCAS(status, kStatusOk, kStatusTimeoutPeer);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // ---------------------------------------------------------------- fences

@@ -106,6 +106,58 @@ int pick_splits(long long tiles, int k_tiles, int sms) {
 
 void check_passes(int64_t passes) { TORCH_CHECK(passes == 1 || passes == 3, "passes must be 1 (tf32) or 3 (3xTF32)"); }
 
+// Tensor-parallel options of one GEMM launch (see Params in gemm_tcgen05.cuh).
+//   wait    = [flags_ptr, operand (0 A / 1 B), epoch, chunk, seq, self]
+//   scatter = [chunk, seq, base_0..base_{P-1}, counter_0..counter_{P-1}]
+struct Comm {
+  std::vector<int64_t> wait;
+  std::vector<int64_t> scatter;
+};
+
+void apply_comm(Params& p, const Comm& cm, bool a_mn, bool b_mn) {
+  if (!cm.wait.empty()) {
+    TORCH_CHECK(cm.wait.size() == 6, "wait spec has 6 entries");
+    TORCH_CHECK(cm.wait[3] > 0 && cm.wait[4] > 0 && cm.wait[4] % cm.wait[3] == 0, "bad gathered chunking");
+    TORCH_CHECK(cm.wait[1] == 0 || b_mn, "a gathered B operand must store tokens along K (MN-major)");
+    (void)a_mn;
+    p.wait_flags = reinterpret_cast<const int*>(cm.wait[0]);
+    p.wait_operand = static_cast<int>(cm.wait[1]);
+    p.wait_epoch = static_cast<int>(cm.wait[2]);
+    p.wait_chunk = static_cast<int>(cm.wait[3]);
+    p.wait_seq = static_cast<int>(cm.wait[4]);
+    p.wait_self = static_cast<int>(cm.wait[5]);
+  }
+  if (!cm.scatter.empty()) {
+    TORCH_CHECK(cm.scatter.size() >= 4 && (cm.scatter.size() - 2) % 2 == 0, "bad scatter spec");
+    const size_t world = (cm.scatter.size() - 2) / 2;
+    TORCH_CHECK(world >= 1 && world <= 8, "scatter over 1..8 ranks");
+    TORCH_CHECK(cm.scatter[0] % BM == 0, "scatter chunk must be a multiple of ", BM, " rows");
+    TORCH_CHECK(cm.scatter[1] == cm.scatter[0] * static_cast<int64_t>(world), "sequence = chunk * ranks");
+    p.scatter_chunk = static_cast<int>(cm.scatter[0]);
+    p.scatter_seq = static_cast<int>(cm.scatter[1]);
+    for (size_t i = 0; i < world; ++i) {
+      TORCH_CHECK(cm.scatter[2 + i] % 16 == 0, "scatter destinations must be 16-byte aligned");
+      p.scatter_base[i] = reinterpret_cast<float*>(cm.scatter[2 + i]);
+      p.scatter_counter[i] = reinterpret_cast<unsigned*>(cm.scatter[2 + world + i]);
+    }
+  }
+}
+
+Comm make_comm(const c10::optional<std::vector<int64_t>>& wait, const c10::optional<std::vector<int64_t>>& scatter) {
+  Comm c;
+  if (wait) c.wait = *wait;
+  if (scatter) c.scatter = *scatter;
+  return c;
+}
+
+int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
+                      int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate,
+                      int64_t passes, const Comm& cm);
+void gemm_swiglu_impl(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
+                      torch::Tensor h, int64_t passes, const Comm& cm);
+void gemm_swiglu_bwd_impl(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u, torch::Tensor dgu,
+                          int64_t passes, const Comm& cm);
+
 }  // namespace
 
 // C = alpha * op(A) @ op(B) [+ residual] [+ C]
@@ -115,6 +167,23 @@ void check_passes(int64_t passes) { TORCH_CHECK(passes == 1 || passes == 3, "pas
 //           2 segmented along K (A columns = concat of K_i)
 void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
               int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate, int64_t passes) {
+  (void)gemm_out_impl(c, a, bs, trans_a, trans_b, b_mode, alpha, residual, accumulate, passes, Comm{});
+}
+
+// gemm_out with the tensor-parallel options: a gathered operand whose rows
+// arrive from peers (wait) and/or an output scattered to the row owners'
+// staging buffers (scatter; no residual / accumulate / split-K then).
+// Returns the output tiles stored on each owner when scattering (0 otherwise).
+int64_t gemm_out_tp(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
+                    int64_t b_mode, double alpha, int64_t passes, c10::optional<std::vector<int64_t>> wait,
+                    c10::optional<std::vector<int64_t>> scatter) {
+  return gemm_out_impl(c, a, bs, trans_a, trans_b, b_mode, alpha, c10::nullopt, false, passes, make_comm(wait, scatter));
+}
+
+namespace {
+int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
+                      int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate,
+                      int64_t passes, const Comm& cm) {
   check_passes(passes);
   TORCH_CHECK(!bs.empty() && bs.size() <= 3, "between 1 and 3 B operands");
   const c10::cuda::CUDAGuard guard(a.device());
@@ -139,13 +208,20 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
     TORCH_CHECK(false, "bad b_mode");
   }
   TORCH_CHECK(c.is_cuda() && c.scalar_type() == torch::kFloat32 && c.dim() == 2 && c.stride(1) == 1, "bad C");
-  TORCH_CHECK(c.size(0) == M && c.size(1) == N, "C shape mismatch");
+  const bool scatter = !cm.scatter.empty();
+  if (scatter) {
+    // C is this rank's staging slice (M / ranks, N): it only fixes the row stride.
+    TORCH_CHECK(c.size(1) == N && c.stride(0) == N, "scatter staging rows must be (.., N) contiguous");
+    TORCH_CHECK(!residual && !accumulate, "scatter GEMMs take no residual / accumulate");
+  } else {
+    TORCH_CHECK(c.size(0) == M && c.size(1) == N, "C shape mismatch");
+  }
   TORCH_CHECK(c.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0, "C must be 16-byte aligned rows");
-  if (M == 0 || N == 0) return;
+  if (M == 0 || N == 0) return 0;
   if (K == 0) {
     if (!accumulate) c.zero_();
     if (residual) c.add_(*residual);
-    return;
+    return 0;
   }
   int BN = pick_bn(N, static_cast<int>(passes));
   if (b_mode == kBSegN && seg % BN != 0) BN = 128;
@@ -171,17 +247,21 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
   }
   p.accumulate = accumulate ? 1 : 0;
   p.status = host::status_ptr(a.device().index());
+  apply_comm(p, cm, A.mn_major, B[0].mn_major);
   const long long tiles = ((M + BM - 1) / BM) * p.num_n_tiles;
   const int k_tiles = static_cast<int>((K + BK - 1) / BK);
   const int sms = at::cuda::getDeviceProperties(a.device().index())->multiProcessorCount;
-  int splits = N % 4 == 0 ? pick_splits(tiles, k_tiles, sms) : 1;
+  int splits = (N % 4 == 0 && !scatter) ? pick_splits(tiles, k_tiles, sms) : 1;
   auto stream = at::cuda::getCurrentCUDAStream();
   p.k_tiles_per_split = (k_tiles + splits - 1) / splits;
   splits = (k_tiles + p.k_tiles_per_split - 1) / p.k_tiles_per_split;
   if (splits == 1) {
     launch_store(p, dim3(static_cast<unsigned>(tiles), 1), BN, A.mn_major, B[0].mn_major, static_cast<int>(passes),
                  stream);
-    return;
+    if (!scatter) return 0;
+    const int64_t owners = (static_cast<int64_t>(cm.scatter.size()) - 2) / 2;
+    TORCH_CHECK(M % (static_cast<int64_t>(BM) * owners) == 0, "scattered rows must split evenly into tiles per owner");
+    return (M / BM / owners) * p.num_n_tiles;
   }
   // Split-K: partials into a workspace, then one deterministic reduction that
   // also applies alpha / residual / accumulate.
@@ -200,7 +280,9 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
       ws.data_ptr<float>(), splits, M, N, p.alpha, p.r, p.ldr, p.accumulate, p.c, p.ldc);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   abacus::host::note_launch();
+  return 0;
 }
+}  // namespace
 
 namespace {
 
@@ -284,6 +366,17 @@ void gemm_batched(torch::Tensor c, torch::Tensor a, torch::Tensor b, bool trans_
 // x (T, D), w_gate / w_up (D, Mh) in the (in, out) layout.
 void gemm_swiglu(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
                  torch::Tensor h, int64_t passes) {
+  gemm_swiglu_impl(x, w_gate, w_up, g, u, h, passes, Comm{});
+}
+
+void gemm_swiglu_tp(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
+                    torch::Tensor h, int64_t passes, std::vector<int64_t> wait) {
+  gemm_swiglu_impl(x, w_gate, w_up, g, u, h, passes, make_comm(wait, c10::nullopt));
+}
+
+namespace {
+void gemm_swiglu_impl(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
+                      torch::Tensor h, int64_t passes, const Comm& cm) {
   check_passes(passes);
   const c10::cuda::CUDAGuard guard(x.device());
   Operand A = operand_of(x, false, "x");
@@ -313,16 +406,29 @@ void gemm_swiglu(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torc
   p.h = h.data_ptr<float>();
   p.ldh = h.stride(0);
   p.status = host::status_ptr(x.device().index());
+  apply_comm(p, cm, false, true);
   p.k_tiles_per_split = static_cast<int>((A.k + BK - 1) / BK);
   const int grid = static_cast<int>(((T + BM - 1) / BM) * p.num_n_tiles);
   auto stream = at::cuda::getCurrentCUDAStream();
   launch_swiglu(p, dim3(grid, 1), BN, static_cast<int>(passes), stream);
 }
+}  // namespace
 
 // SwiGLU backward through the hidden layer: dh = dy @ w_down^T, then
 // dgu[:, :Mh] = dh * u * silu'(g), dgu[:, Mh:] = dh * silu(g).
 void gemm_swiglu_bwd(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u, torch::Tensor dgu,
                      int64_t passes) {
+  gemm_swiglu_bwd_impl(dy, w_down, g, u, dgu, passes, Comm{});
+}
+
+void gemm_swiglu_bwd_tp(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u, torch::Tensor dgu,
+                        int64_t passes, std::vector<int64_t> wait) {
+  gemm_swiglu_bwd_impl(dy, w_down, g, u, dgu, passes, make_comm(wait, c10::nullopt));
+}
+
+namespace {
+void gemm_swiglu_bwd_impl(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u, torch::Tensor dgu,
+                          int64_t passes, const Comm& cm) {
   check_passes(passes);
   const c10::cuda::CUDAGuard guard(dy.device());
   Operand A = operand_of(dy, false, "dy");
@@ -350,11 +456,13 @@ void gemm_swiglu_bwd(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, to
   p.dgu = dgu.data_ptr<float>();
   p.ld_dgu = dgu.stride(0);
   p.status = host::status_ptr(dy.device().index());
+  apply_comm(p, cm, false, false);
   p.k_tiles_per_split = static_cast<int>((A.k + BK - 1) / BK);
   const int grid = static_cast<int>(((T + BM - 1) / BM) * p.num_n_tiles);
   auto stream = at::cuda::getCurrentCUDAStream();
   launch_swiglu_bwd(p, dim3(grid, 1), BN, static_cast<int>(passes), stream);
 }
+}  // namespace
 
 }  // namespace gemm
 }  // namespace abacus

@@ -69,8 +69,39 @@ struct alignas(64) Params {
   //   2: K range [0, m0 + BM)   (P @ V, dS @ K: keys after the last query)
   //   3: K range [m0, K)        (dS^T @ Q, P^T @ dO: queries before the first key)
   int causal;
+  // Tensor-parallel all-gather fused into the GEMM: the gathered operand
+  // (A when wait_operand == 0, else B) holds rows pushed by the ranks that own
+  // them, `wait_chunk` rows per rank inside every `wait_seq`-row sequence. A
+  // CTA starts only once each owner of the rows it reads has published
+  // `wait_epoch` in wait_flags[owner]; rows of this rank (wait_self) are local.
+  const int* wait_flags;
+  int wait_operand;
+  int wait_epoch, wait_chunk, wait_seq, wait_self;
+  // GEMM -> reduce-scatter: output row r is stored on rank (r % seq) / chunk,
+  // into this rank's slot of that rank's staging buffer (scatter_base[owner]),
+  // at row (r / seq) * chunk + r % chunk; every finished tile then adds 1 to
+  // the owner's arrival counter for this rank (release, system scope).
+  float* scatter_base[8];
+  unsigned* scatter_counter[8];
+  int scatter_chunk, scatter_seq;
   int* status;
 };
+
+// Wait (bounded) until every owner of stored rows [r0, r1) of the gathered
+// operand has published the expected epoch.
+__device__ __forceinline__ bool wait_gathered_rows(const Params& p, int r0, int r1) {
+  unsigned done = 0;
+  for (int r = r0; r < r1;) {
+    const int pos = r % p.wait_seq;
+    const int owner = pos / p.wait_chunk;
+    if (owner != p.wait_self && !(done & (1u << owner))) {
+      if (!wait_flag_geq(p.wait_flags + owner, p.wait_epoch, p.status)) return false;
+      done |= 1u << owner;
+    }
+    r += p.wait_chunk - pos % p.wait_chunk;
+  }
+  return true;
+}
 
 template <int BN, bool A_MN, bool B_MN, int PASSES, int STAGES>
 struct Config {
@@ -144,6 +175,19 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   const int num_k = max(0, min(total_k, kt_begin + p.k_tiles_per_split) - kt_begin);
   const int bz_h = p.batched ? static_cast<int>(blockIdx.z) % p.batch_h : 0;
   const int bz_b = p.batched ? static_cast<int>(blockIdx.z) / p.batch_h : 0;
+  if (p.wait_flags != nullptr) {
+    // Rows of the gathered operand this CTA reads: the M range for a K-major
+    // A, else the K range (MN-major A or B store tokens along K).
+    __shared__ int wait_ok;
+    if (threadIdx.x == 0) {
+      const bool rows_are_m = p.wait_operand == 0 && !A_MN;
+      const int r0 = rows_are_m ? m0 : kt_begin * BK;
+      const int r1 = rows_are_m ? min(m0 + BM, p.M) : min((kt_begin + num_k) * BK, p.K);
+      wait_ok = wait_gathered_rows(p, r0, r1) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!wait_ok) return;
+  }
   auto load = [&](void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
     if (p.batched) tma_load_4d(dst, map, bar, x, y, bz_h, bz_b);
     else tma_load_2d(dst, map, bar, x, y);
@@ -345,8 +389,17 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
         group(c, v);
         const int col0 = n0 + c * 32;
         if (row_ok && col0 < p.N) {
-          float* crow = p.c + blockIdx.y * p.split_stride + bz_b * p.c_stride_b + bz_h * p.c_stride_h +
-                        static_cast<long long>(row) * p.ldc + col0;
+          float* crow;
+          if (p.scatter_chunk) {
+            const int pos = row % p.scatter_seq;
+            const int owner = pos / p.scatter_chunk;
+            const long long lrow =
+                static_cast<long long>(row / p.scatter_seq) * p.scatter_chunk + (pos - owner * p.scatter_chunk);
+            crow = p.scatter_base[owner] + lrow * p.ldc + col0;
+          } else {
+            crow = p.c + blockIdx.y * p.split_stride + bz_b * p.c_stride_b + bz_h * p.c_stride_h +
+                   static_cast<long long>(row) * p.ldc + col0;
+          }
           const float* rrow = p.r ? p.r + static_cast<long long>(row) * p.ldr + col0 : nullptr;
           if (col0 + 32 <= p.N) {
 #pragma unroll
@@ -415,6 +468,17 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
             }
           }
         }
+      }
+    }
+    if (EPI == kEpiStore && p.scatter_chunk) {
+      // Publish this tile to its owner once all four epilogue warps stored it.
+      __shared__ int epi_ok[4];
+      __threadfence_system();
+      if (lane == 0) epi_ok[q] = ok ? 1 : 0;
+      named_barrier_sync(1, 128);
+      if (warp == 2 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
+        const int owner = (m0 % p.scatter_seq) / p.scatter_chunk;
+        red_release_sys_add(p.scatter_counter[owner], 1u);
       }
     }
   } else if (PASSES == 3 && warp >= 6) {

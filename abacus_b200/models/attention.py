@@ -24,7 +24,7 @@ import torch
 from abacus_b200.models.layers import RMSNorm, Rotary, apply_rotary_pos_emb
 from abacus_b200.ops import attention as attn_ops
 from abacus_b200.ops import gemm
-from abacus_b200.parallel import mesh
+from abacus_b200.parallel import mesh, tp_fused
 from abacus_b200.parallel.context_parallel import (
     _AllGatherSequenceBlock,
     all_gather_positions,
@@ -108,6 +108,7 @@ class MultiHeadAttention(torch.nn.Module):
         self.w_k_DHK = torch.nn.Parameter(k_DHK[:, start : start + self.local_heads].clone())
         self.w_v_DHK = torch.nn.Parameter(v_DHK[:, start : start + self.local_heads].clone())
         self.w_o_HKD = torch.nn.Parameter(o_HKD[start : start + self.local_heads].clone())
+        self._tp_key = tp_fused.new_key("attn") if tensor_parallel and sequence_parallel else None
         # One gamma shared by all heads; summed over TP ranks (heads sharded).
         self.q_norm = RMSNorm(head_dim, sync_grads=tensor_parallel)
         self.k_norm = RMSNorm(head_dim, sync_grads=tensor_parallel)
@@ -118,6 +119,8 @@ class MultiHeadAttention(torch.nn.Module):
         into the O-projection epilogue on one rank)."""
         if self.context_parallel:
             return self._forward_context_parallel(x_BLD, rotary, residual)
+        if self._tp_fused_usable(x_BLD, rotary, residual):
+            return self._forward_tp_fused(x_BLD, rotary, residual)
         if self.world_size > 1 and self.sequence_parallel:
             x_BLD = _GatherFromSequenceParallel.apply(x_BLD, "tp")
         elif self.world_size > 1:
@@ -136,6 +139,22 @@ class MultiHeadAttention(torch.nn.Module):
         if residual is not None and not fuse_residual:
             out = residual + out
         return out
+
+    def _tp_fused_usable(self, x_BLD, rotary, residual) -> bool:
+        return (self.world_size > 1 and self.sequence_parallel and residual is not None and rotary is not None
+                and (self.local_heads * self.head_dim) % 128 == 0 and tp_fused.usable(x_BLD, x_BLD.shape[1]))
+
+    def _forward_tp_fused(self, x_BLD, rotary, residual):
+        """SP shard -> (gather fused into the QKV GEMM) -> attention on the local
+        heads -> (O-projection GEMM scattering its rows to their owners) ->
+        residual + reduce, all over NVLink peer memory."""
+        b = x_BLD.shape[0]
+        qkv = tp_fused.gather_qkv(x_BLD, self.w_q_DHK, self.w_k_DHK, self.w_v_DHK, self._tp_key)
+        o = attn_ops.causal_attention(
+            qkv, b, self.local_heads, self.head_dim, self.q_norm.gamma(), self.k_norm.gamma(), rotary.inv_freq
+        )
+        w_o = self.w_o_HKD.reshape(self.local_heads * self.head_dim, self.dim)
+        return tp_fused.row_scatter(o, w_o, residual, self._tp_key)
 
     def _forward_fused(self, x_BLD, rotary, residual):
         b, length, _ = x_BLD.shape

@@ -17,7 +17,7 @@ import torch
 from abacus_b200.ops import embedding as embedding_ops
 from abacus_b200.ops import gemm
 from abacus_b200.ops.norm import rmsnorm
-from abacus_b200.parallel import mesh
+from abacus_b200.parallel import mesh, tp_fused
 from abacus_b200.parallel.tensor_parallel import (
     _AllReduceGrads,
     _GatherFromSequenceParallel,
@@ -142,8 +142,20 @@ class MLPTensorParallel(torch.nn.Module):
         self.w_gate_DM = torch.nn.Parameter(gate_DM[:, start : start + local_hidden].clone())
         self.w_up_DM = torch.nn.Parameter(up_DM[:, start : start + local_hidden].clone())
         self.w_down_MD = torch.nn.Parameter(down_MD[start : start + local_hidden].clone())
+        self._tp_key = tp_fused.new_key("mlp") if sequence_parallel else None
 
-    def forward(self, x_BLD: torch.Tensor) -> torch.Tensor:
+    def forward(self, x_BLD: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """Partial-sum-free output (B, l or L, D); ``residual`` is added when given."""
+        if (residual is not None and self.world_size > 1 and self.sequence_parallel
+                and (self.hidden_dim // self.world_size) % 32 == 0 and tp_fused.usable(x_BLD, x_BLD.shape[1], self.dim_name)):
+            # Gather fused into the gate/up GEMM, reduce-scatter fused into the
+            # down GEMM's epilogue, residual added in the reduction.
+            return tp_fused.swiglu(x_BLD, self.w_gate_DM, self.w_up_DM, self.w_down_MD, residual, self._tp_key,
+                                   self.dim_name)
+        out = self._forward_unfused(x_BLD)
+        return out if residual is None else residual + out
+
+    def _forward_unfused(self, x_BLD: torch.Tensor) -> torch.Tensor:
         if self.world_size > 1 and self.sequence_parallel:
             x_BLD = _GatherFromSequenceParallel.apply(x_BLD, self.dim_name)
         elif self.world_size > 1:

@@ -21,7 +21,7 @@ from abacus_b200.models.attention import MultiHeadAttention
 from abacus_b200.models.layers import MLP, Embedding, MLPTensorParallel, RMSNorm, Rotary
 from abacus_b200.ops import gemm
 from abacus_b200.ops.cross_entropy import fused_linear_cross_entropy
-from abacus_b200.parallel import mesh
+from abacus_b200.parallel import mesh, tp_fused
 from abacus_b200.parallel.context_parallel import zigzag_positions
 from abacus_b200.parallel.tensor_parallel import _GatherReplicated, _ScatterToSequenceParallel
 
@@ -62,9 +62,7 @@ class TransformerBlock(torch.nn.Module):
     def forward(self, x_BLD: torch.Tensor, rotary: torch.nn.Module | None = None) -> torch.Tensor:
         if not self._dropout_active():
             x_BLD = self.attention(self.norm_attention(x_BLD), rotary, residual=x_BLD)
-            if isinstance(self.mlp, MLP):
-                return self.mlp(self.norm_mlp(x_BLD), residual=x_BLD)
-            return x_BLD + self.mlp(self.norm_mlp(x_BLD))
+            return self.mlp(self.norm_mlp(x_BLD), residual=x_BLD)
         x_BLD = x_BLD + self.dropout(self.attention(self.norm_attention(x_BLD), rotary))
         return x_BLD + self.dropout(self.mlp(self.norm_mlp(x_BLD)))
 
@@ -135,6 +133,10 @@ class Transformer(torch.nn.Module):
             if world > 1:
                 positions = zigzag_positions(tokens_BL.shape[1], rank, world)
                 tokens_BL = tokens_BL.index_select(1, positions.to(tokens_BL.device))
+        if self.sequence_parallel and self.world_size > 1 and tokens_BL.is_cuda:
+            # Fused TP buffers are reused every step: wait (bounded, on the
+            # device) until every TP rank finished the previous step.
+            tp_fused.begin_step(tokens_BL.device)
         x_BLD = self.embedding(tokens_BL)
         if self.sequence_parallel and self.world_size > 1:
             x_BLD = _ScatterToSequenceParallel.apply(x_BLD, "tp")

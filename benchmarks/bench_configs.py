@@ -10,8 +10,10 @@ between barrier + synchronize, CUDA events, max over ranks; one JSON line):
 * ``tp``: ~1.3B dense GPT, 24 layers, d_model 2048, 16 heads x 128, SwiGLU
   5632, vocab 50304, seq_len 2048, global batch 16, tensor parallel TP=N with
   Megatron sequence parallel (every TP rank sees the whole batch).
-  Reference arm: the reference's own TP+SP Transformer with its
-  MLPTensorParallel resized to 5632 (it hard-codes the hidden size).
+  Reference arm: the reference's own TP Transformer with its
+  MLPTensorParallel resized to 5632 (it hard-codes the hidden size), without
+  sequence parallel: its SP gather calls ``dist.all_gather_single``, which
+  torch 2.11 does not provide.
 * ``moe``: 12 layers, d_model 768, 12 heads x 64, 8 SwiGLU experts of
   hidden 1536 in every layer, softmax top-2 router with load-balancing loss and
   capacity factor 1.25, vocab 50304, seq_len 1024, global batch 64. Experts
@@ -120,17 +122,19 @@ def build_reference(cfg, args, world, device):
         from abacus.mlp import MLPTensorParallel  # noqa: PLC0415
         from abacus.transformer import Transformer  # noqa: PLC0415
 
+        # The reference's sequence-parallel gather calls dist.all_gather_single,
+        # which this torch does not have, so its arm runs TP without SP.
         model = Transformer(dim=2048, n_heads=16, head_dim=128, n_blocks=args.layers or 24, vocab_size=VOCAB,
-                            tensor_parallel=world > 1, sequence_parallel=world > 1)
+                            tensor_parallel=world > 1, sequence_parallel=False)
         if world > 1:
             for block in model.blocks:
-                block.mlp = MLPTensorParallel(2048, 5632, sequence_parallel=True)
+                block.mlp = MLPTensorParallel(2048, 5632, sequence_parallel=False)
         else:
             from abacus.mlp import MLP  # noqa: PLC0415
 
             for block in model.blocks:
                 block.mlp = MLP(2048, 5632)
-        return Trainer(model.to(device), total_steps=1000), None, "tp%d+sp" % world, True
+        return Trainer(model.to(device), total_steps=1000), None, "tp%d (no SP)" % world, True
     if world not in (1, 8):
         return None, "the reference's expert parallel keeps one expert per rank: 8 experts need 1 or 8 ranks", None, None
     from abacus.transformer_moe import TransformerMoe  # noqa: PLC0415

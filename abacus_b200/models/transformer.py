@@ -23,7 +23,12 @@ from abacus_b200.ops import gemm
 from abacus_b200.ops.cross_entropy import fused_linear_cross_entropy
 from abacus_b200.parallel import mesh, tp_fused
 from abacus_b200.parallel.context_parallel import zigzag_positions
-from abacus_b200.parallel.tensor_parallel import _GatherReplicated, _ScatterToSequenceParallel
+from abacus_b200.parallel.tensor_parallel import (
+    _AllReduceGrads,
+    _GatherReplicated,
+    _ScatterToSequenceParallel,
+    _SumOutputs,
+)
 
 
 class TransformerBlock(torch.nn.Module):
@@ -124,6 +129,13 @@ class Transformer(torch.nn.Module):
 
     def hidden_states(self, tokens_BL: torch.Tensor) -> torch.Tensor:
         """Final-norm output (B, L, D) (replicated over SP ranks)."""
+        x_BLD = self._final_norm(tokens_BL)
+        if self.sequence_parallel and self.world_size > 1:
+            x_BLD = _GatherReplicated.apply(x_BLD, "tp")
+        return x_BLD
+
+    def _final_norm(self, tokens_BL: torch.Tensor) -> torch.Tensor:
+        """Final-norm output: (B, L, D), or this rank's (B, L/P, D) shard under SP."""
         if self.sequence_parallel and self.world_size > 1:
             length = tokens_BL.shape[1]
             if length % self.world_size != 0:
@@ -142,13 +154,26 @@ class Transformer(torch.nn.Module):
             x_BLD = _ScatterToSequenceParallel.apply(x_BLD, "tp")
         for block in self.blocks:
             x_BLD = block(x_BLD, self.rotary)
-        x_BLD = self.norm(x_BLD)
-        if self.sequence_parallel and self.world_size > 1:
-            x_BLD = _GatherReplicated.apply(x_BLD, "tp")
-        return x_BLD
+        return self.norm(x_BLD)
 
     def forward(self, tokens_BL: torch.Tensor, targets=None, normalizer=None) -> torch.Tensor:
-        """Logits (B, L, V); with ``targets`` (B, L) the scalar training loss."""
+        """Logits (B, L, V); with ``targets`` (B, L) the scalar training loss.
+
+        Under sequence parallel the loss is computed on each rank's own
+        sequence shard (no gather of the final hidden states) and summed over
+        the TP group; the head weight's gradient is summed over the group in
+        backward. Same value and gradients as the reference's replicated head
+        (``abacus/transformer.py:80-97``), 1/P of its work per rank.
+        """
+        if targets is not None and self.sequence_parallel and self.world_size > 1:
+            rank, _ = mesh.rank_and_world_size("tp")
+            x_BlD = self._final_norm(tokens_BL)
+            chunk = x_BlD.shape[1]
+            if normalizer is None:
+                normalizer = (targets != -100).sum().to(torch.float32)
+            weight = _AllReduceGrads.apply(self.w_D_vocab, "tp")
+            partial = _head(x_BlD, weight, targets[:, rank * chunk : (rank + 1) * chunk], normalizer)
+            return _SumOutputs.apply(partial, "tp")
         return _head(self.hidden_states(tokens_BL), self.w_D_vocab, targets, normalizer)
 
 

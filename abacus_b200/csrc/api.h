@@ -51,6 +51,15 @@ namespace abacus {
 namespace attn {
 void causal_softmax_fwd(torch::Tensor s);
 void causal_softmax_bwd(torch::Tensor p, torch::Tensor dp, double scale);
+void flash_attn_fwd_cp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                       int64_t batch, int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
+                       c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes,
+                       std::vector<int64_t> wait);
+void flash_attn_bwd_cp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor dout,
+                       torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, int64_t batch,
+                       int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
+                       c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes,
+                       std::vector<int64_t> scatter);
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                     int64_t batch, int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes);

@@ -54,9 +54,39 @@ const int64_t* positions_ptr(const c10::optional<torch::Tensor>& pos, int64_t le
 
 }  // namespace
 
+namespace {
+void flash_fwd_impl(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                    int64_t batch, int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
+                    c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes,
+                    const std::vector<int64_t>& wait);
+void flash_bwd_impl(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor dout,
+                    torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, int64_t batch,
+                    int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
+                    c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes,
+                    const std::vector<int64_t>& scatter);
+}  // namespace
+
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                     int64_t batch, int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes) {
+  flash_fwd_impl(q, k, v, out, lse, batch, heads, head_dim, lq, lk, scale, q_pos, k_pos, passes, {});
+}
+
+// Context-parallel forward: K / V are the gathered buffers every rank pushes
+// its shard into; wait = [flags_ptr, epoch, ranks, self].
+void flash_attn_fwd_cp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                       int64_t batch, int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
+                       c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes,
+                       std::vector<int64_t> wait) {
+  TORCH_CHECK(wait.size() == 4, "wait = [flags, epoch, ranks, self]");
+  flash_fwd_impl(q, k, v, out, lse, batch, heads, head_dim, lq, lk, scale, q_pos, k_pos, passes, wait);
+}
+
+namespace {
+void flash_fwd_impl(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                    int64_t batch, int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
+                    c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes,
+                    const std::vector<int64_t>& wait) {
   const c10::cuda::CUDAGuard guard(q.device());
   TORCH_CHECK(passes == 1 || passes == 3, "passes must be 1 or 3");
   TORCH_CHECK(head_dim == 64 || (head_dim == 128 && passes == 1) || (head_dim == 32),
@@ -86,6 +116,13 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
   p.lk = static_cast<int>(lk);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.status = host::status_ptr(q.device().index());
+  if (!wait.empty()) {
+    TORCH_CHECK(wait[2] >= 1 && wait[2] <= 8 && wait[3] >= 0 && wait[3] < wait[2], "bad wait spec");
+    p.wait_flags = reinterpret_cast<const int*>(wait[0]);
+    p.wait_epoch = static_cast<int>(wait[1]);
+    p.wait_world = static_cast<int>(wait[2]);
+    p.wait_self = static_cast<int>(wait[3]);
+  }
   dim3 grid(static_cast<unsigned>((lq + kBlockM - 1) / kBlockM), static_cast<unsigned>(heads),
             static_cast<unsigned>(batch));
   auto s = at::cuda::getCurrentCUDAStream();
@@ -99,6 +136,7 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
     launch_fwd<128, 1>(p, grid, s);
   }
 }
+}  // namespace
 
 namespace {
 
@@ -180,6 +218,29 @@ void flash_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, int64_t batch,
                     int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes) {
+  flash_bwd_impl(q, k, v, out, dout, lse, dq, dk, dv, batch, heads, head_dim, lq, lk, scale, q_pos, k_pos, passes,
+                 {});
+}
+
+// Context-parallel backward: dK / dV of the gathered keys are stored straight
+// into their owners' staging slots (dk / dv here are this rank's slot views,
+// which fix the row stride); scatter = [chunk, dk_0.., dv_0.., counter_0..].
+void flash_attn_bwd_cp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor dout,
+                       torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, int64_t batch,
+                       int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
+                       c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes,
+                       std::vector<int64_t> scatter) {
+  TORCH_CHECK(scatter.size() >= 4 && (scatter.size() - 1) % 3 == 0, "scatter = [chunk, dk.., dv.., counters..]");
+  flash_bwd_impl(q, k, v, out, dout, lse, dq, dk, dv, batch, heads, head_dim, lq, lk, scale, q_pos, k_pos, passes,
+                 scatter);
+}
+
+namespace {
+void flash_bwd_impl(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor dout,
+                    torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, int64_t batch,
+                    int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
+                    c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes,
+                    const std::vector<int64_t>& scatter) {
   const c10::cuda::CUDAGuard guard(q.device());
   TORCH_CHECK(passes == 1 || passes == 3, "passes must be 1 or 3");
   TORCH_CHECK(head_dim == 64 || head_dim == 32 || (head_dim == 128 && passes == 1),
@@ -218,6 +279,18 @@ void flash_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
   p.scale = static_cast<float>(scale);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.status = host::status_ptr(q.device().index());
+  if (!scatter.empty()) {
+    const size_t world = (scatter.size() - 1) / 3;
+    TORCH_CHECK(world >= 1 && world <= 8, "scatter over 1..8 ranks");
+    TORCH_CHECK(scatter[0] % 128 == 0 && scatter[0] * static_cast<int64_t>(world) == lk,
+                "key chunk must be a multiple of 128 and cover the gathered keys");
+    p.scatter_chunk = static_cast<int>(scatter[0]);
+    for (size_t i = 0; i < world; ++i) {
+      p.scatter_dk[i] = reinterpret_cast<float*>(scatter[1 + i]);
+      p.scatter_dv[i] = reinterpret_cast<float*>(scatter[1 + world + i]);
+      p.scatter_counter[i] = reinterpret_cast<unsigned*>(scatter[1 + 2 * world + i]);
+    }
+  }
   const int LQ = static_cast<int>(lq), LK = static_cast<int>(lk);
   if (head_dim == 64) {
     if (passes == 3) run_bwd<64, 3>(p, q, k, v, dout, LQ, LK, s);
@@ -229,6 +302,7 @@ void flash_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
     run_bwd<128, 1>(p, q, k, v, dout, LQ, LK, s);
   }
 }
+}  // namespace
 
 }  // namespace attn
 }  // namespace abacus

@@ -48,6 +48,14 @@ struct BwdParams {
   int batch, heads, lq, lk;
   float scale;         // softmax scale
   float scale_log2;    // scale * log2(e)
+  // Context parallel: dK / dV rows of the gathered keys go to their owner's
+  // staging slot (row (b*lk + k) -> owner k / chunk, local row b*chunk +
+  // k % chunk, row stride ld_dk / ld_dv) and each finished 128-key tile adds
+  // 1 to the owner's arrival counter (scatter_chunk 0: plain stores).
+  float* scatter_dk[8];
+  float* scatter_dv[8];
+  unsigned* scatter_counter[8];
+  int scatter_chunk;
   int* status;
 };
 
@@ -391,8 +399,17 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
     // TMEM loads are warp-collective: every lane loads, only valid rows store.
     const bool have = __all_sync(0xffffffffu, ok) && nb > 0;
     {
-      float* dvrow = p.dv + static_cast<long long>(b * p.lk + ki) * p.ld_dv + col0;
-      float* dkrow = p.dk + static_cast<long long>(b * p.lk + ki) * p.ld_dk + col0;
+      float* dvrow;
+      float* dkrow;
+      if (p.scatter_chunk) {
+        const int owner = min(ki, p.lk - 1) / p.scatter_chunk;
+        const long long lrow = static_cast<long long>(b) * p.scatter_chunk + (ki - owner * p.scatter_chunk);
+        dvrow = p.scatter_dv[owner] + lrow * p.ld_dv + col0;
+        dkrow = p.scatter_dk[owner] + lrow * p.ld_dk + col0;
+      } else {
+        dvrow = p.dv + static_cast<long long>(b * p.lk + ki) * p.ld_dv + col0;
+        dkrow = p.dk + static_cast<long long>(b * p.lk + ki) * p.ld_dk + col0;
+      }
       const int vcol = PASSES == 3 ? Cfg::kDVm : Cfg::kDVp;
       const int kcol = PASSES == 3 ? Cfg::kDKm : Cfg::kDKp;
 #pragma unroll
@@ -415,6 +432,17 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
               make_float4(__uint_as_float(g[t]) * p.scale, __uint_as_float(g[t + 1]) * p.scale,
                           __uint_as_float(g[t + 2]) * p.scale, __uint_as_float(g[t + 3]) * p.scale);
         }
+      }
+    }
+    if (p.scatter_chunk) {
+      // Publish this 128-key tile to its owner once all four warps stored it.
+      __shared__ int tile_ok[4];
+      __threadfence_system();
+      const bool warp_ok = __all_sync(0xffffffffu, ok);
+      if (lane == 0) tile_ok[warp % 4] = warp_ok ? 1 : 0;
+      named_barrier_sync(1, 128);
+      if (warp == 2 && lane == 0 && tile_ok[0] && tile_ok[1] && tile_ok[2] && tile_ok[3]) {
+        red_release_sys_add(p.scatter_counter[k0 / p.scatter_chunk], 1u);
       }
     }
   } else if (PASSES == 3) {

@@ -46,6 +46,10 @@ struct FwdParams {
   const int64_t* k_pos;  // (Lk,) or null
   int batch, heads, lq, lk;
   float scale_log2;    // softmax scale * log2(e)
+  // Context parallel: K / V rows are pushed here by their owning ranks; a CTA
+  // starts once every other rank published `wait_epoch` (null: no wait).
+  const int* wait_flags;
+  int wait_epoch, wait_world, wait_self;
   int* status;
 };
 
@@ -85,7 +89,17 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
   // Abort early (uniformly for the whole CTA) if an earlier kernel on this
   // device already recorded an error.
   __shared__ int abort_flag;
-  if (threadIdx.x == 0) abort_flag = *reinterpret_cast<volatile int*>(p.status);
+  if (threadIdx.x == 0) {
+    abort_flag = *reinterpret_cast<volatile int*>(p.status);
+    if (abort_flag == kStatusOk && p.wait_flags != nullptr) {
+      for (int r = 0; r < p.wait_world; ++r) {
+        if (r != p.wait_self && !wait_flag_geq(p.wait_flags + r, p.wait_epoch, p.status)) {
+          abort_flag = kStatusTimeoutPeer;
+          break;
+        }
+      }
+    }
+  }
   __syncthreads();
   if (abort_flag != kStatusOk) return;
   const uint32_t raw = smem_u32(smem_raw);

@@ -22,6 +22,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &abacus::ops::adamw_step);
   m.def("causal_softmax_fwd", &abacus::attn::causal_softmax_fwd, "in-place causal row softmax (materialised attention)");
   m.def("causal_softmax_bwd", &abacus::attn::causal_softmax_bwd, "in-place dS from P and dP (materialised attention)");
+  m.def("flash_attn_fwd_cp", &abacus::attn::flash_attn_fwd_cp, "flash forward over peer-pushed K/V (context parallel)");
+  m.def("flash_attn_bwd_cp", &abacus::attn::flash_attn_bwd_cp, "flash backward scattering dK/dV to their owners");
   m.def("flash_attn_fwd", &abacus::attn::flash_attn_fwd);
   m.def("flash_attn_bwd", &abacus::attn::flash_attn_bwd);
   m.def("launch_count", &abacus::host::launch_count, "number of abacus kernels launched by this process");

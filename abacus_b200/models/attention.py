@@ -24,7 +24,7 @@ import torch
 from abacus_b200.models.layers import RMSNorm, Rotary, apply_rotary_pos_emb
 from abacus_b200.ops import attention as attn_ops
 from abacus_b200.ops import gemm
-from abacus_b200.parallel import mesh, tp_fused
+from abacus_b200.parallel import cp_fused, mesh, tp_fused
 from abacus_b200.parallel.context_parallel import (
     _AllGatherSequenceBlock,
     all_gather_positions,
@@ -109,6 +109,7 @@ class MultiHeadAttention(torch.nn.Module):
         self.w_v_DHK = torch.nn.Parameter(v_DHK[:, start : start + self.local_heads].clone())
         self.w_o_HKD = torch.nn.Parameter(o_HKD[start : start + self.local_heads].clone())
         self._tp_key = tp_fused.new_key("attn") if tensor_parallel and sequence_parallel else None
+        self._cp_key = tp_fused.new_key("cpattn") if context_parallel else None
         # One gamma shared by all heads; summed over TP ranks (heads sharded).
         self.q_norm = RMSNorm(head_dim, sync_grads=tensor_parallel)
         self.k_norm = RMSNorm(head_dim, sync_grads=tensor_parallel)
@@ -191,10 +192,16 @@ class MultiHeadAttention(torch.nn.Module):
                 rotary.inv_freq, local_len, positions=token_pos, n_positions=local_len * world,
             )
             hk = self.local_heads * self.head_dim
-            k = _GatherFromSequenceParallel.apply(k.view(b, local_len, hk), "cp").reshape(-1, hk)
-            v = _GatherFromSequenceParallel.apply(v.reshape(b, local_len, hk), "cp").reshape(-1, hk)
             k_pos = all_gather_positions(positions)
-            o = attn_ops.flash_attention(q, k, v, b, self.local_heads, self.head_dim, q_pos=positions, k_pos=k_pos)
+            if world > 1 and cp_fused.usable(x_BLD, local_len, self.head_dim):
+                # K/V gather fused into the flash kernel's loads, dK/dV
+                # reduce-scatter into its backward stores (NVLink peer memory).
+                o = cp_fused.attention(q, k, v, b, self.local_heads, self.head_dim, positions, k_pos, self._cp_key)
+            else:
+                k = _GatherFromSequenceParallel.apply(k.view(b, local_len, hk), "cp").reshape(-1, hk)
+                v = _GatherFromSequenceParallel.apply(v.reshape(b, local_len, hk), "cp").reshape(-1, hk)
+                o = attn_ops.flash_attention(q, k, v, b, self.local_heads, self.head_dim, q_pos=positions,
+                                             k_pos=k_pos)
             w_o = self.w_o_HKD.reshape(hk, self.dim)
             res2 = None if residual is None else residual.reshape(-1, self.dim)
             return gemm.linear(o, w_o, res2).view(b, local_len, self.dim)

@@ -21,7 +21,7 @@ from abacus_b200.models.attention import MultiHeadAttention
 from abacus_b200.models.layers import MLP, Embedding, MLPTensorParallel, RMSNorm, Rotary
 from abacus_b200.ops import gemm
 from abacus_b200.ops.cross_entropy import fused_linear_cross_entropy
-from abacus_b200.parallel import mesh, tp_fused
+from abacus_b200.parallel import cp_fused, mesh, tp_fused
 from abacus_b200.parallel.context_parallel import zigzag_positions
 from abacus_b200.parallel.tensor_parallel import (
     _AllReduceGrads,
@@ -145,6 +145,8 @@ class Transformer(torch.nn.Module):
             if world > 1:
                 positions = zigzag_positions(tokens_BL.shape[1], rank, world)
                 tokens_BL = tokens_BL.index_select(1, positions.to(tokens_BL.device))
+                if tokens_BL.is_cuda:
+                    cp_fused.begin_step(tokens_BL.device)
         if self.sequence_parallel and self.world_size > 1 and tokens_BL.is_cuda:
             # Fused TP buffers are reused every step: wait (bounded, on the
             # device) until every TP rank finished the previous step.

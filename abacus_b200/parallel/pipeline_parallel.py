@@ -72,6 +72,12 @@ class PipelineParallel:
         total = (targets_all != IGNORE).sum().to(torch.float32)
         if cp:
             dist.all_reduce(total, op=dist.ReduceOp.SUM, group=mesh.group_for("cp"))
+            if tokens_BL.is_cuda:
+                from abacus_b200.parallel import cp_fused
+
+                # Fused CP buffers are keyed per microbatch call and reused every
+                # step: bounded device barrier over the CP group first.
+                cp_fused.begin_step(tokens_BL.device)
         if not tokens_BL.is_cuda and total.item() < 1:
             raise ValueError("batch has no target tokens")
 

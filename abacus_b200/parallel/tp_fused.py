@@ -18,11 +18,12 @@ separate NCCL call between GEMMs; here:
   remaining tiles' math; ``tp_reduce_rows`` then sums the slots in rank
   order and adds the residual stream in the same pass.
 
-Buffers are symmetric-memory allocations keyed per layer and role, created on
-first use (every TP rank creates the same keys in the same order). A bounded
-device barrier at the start of each forward (``begin_step``) keeps a rank
-from pushing into a buffer a slower peer may still read from the previous
-step's backward.
+Buffers are symmetric-memory allocations keyed per layer, role and call
+within the step (microbatches that run forward before any backward each get
+their own), created on first use: every TP rank creates the same keys in the
+same order. A bounded device barrier when a new step starts (``begin_step``)
+keeps a rank from pushing into a buffer a slower peer may still read from the
+previous step's backward.
 
 Requirements (else the NCCL path in ``tensor_parallel`` runs): CUDA fp32,
 2..8 ranks, per-rank sequence chunk a multiple of 128 rows.
@@ -74,6 +75,8 @@ class Workspace:
         self._epochs: dict[str, int] = {}
         self._targets: dict[str, int] = {}
         self._done: dict[str, torch.Tensor] = {}
+        self._calls: dict[str, int] = {}
+        self._backward_seen = False
         self._barrier_epoch = 0
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)
@@ -120,7 +123,24 @@ class Workspace:
         self._targets[key] = t
         return t
 
+    def call_key(self, key: str) -> str:
+        """Key of this call of a module since the step began: every microbatch
+        of a pipeline step gets its own buffers (backward reuses the key its
+        forward saved)."""
+        n = self._calls.get(key, 0)
+        self._calls[key] = n + 1
+        return f"{key}#{n}"
+
     def begin_step(self, timeout_ms: float = 60_000.0) -> None:
+        """Called at every forward. A forward that follows a backward (or runs
+        without autograd) starts a new step: call keys restart at 0, so the
+        buffers are reused, after a bounded device barrier that every rank
+        reaches only once its previous work finished. Further forwards before
+        the next backward (microbatches) take fresh keys and need no barrier."""
+        if self._calls and not self._backward_seen and torch.is_grad_enabled():
+            return
+        self._calls.clear()
+        self._backward_seen = False
         self._barrier_epoch += 1
         ext().symm_barrier(self.signal_ptrs, self.rank, 0, self._barrier_epoch, timeout_ms, [], None)
 
@@ -204,6 +224,7 @@ class _GatherQKV(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x2, wq, wk, wv, key, chunk, seq, dim):
         ws = workspace(x2.device, dim)
+        key = ws.call_key(key)
         gathered, spec = ws.push_gather(key + ".G", x2, chunk, seq)
         mats = [w.reshape(w.shape[0], -1) for w in (wq, wk, wv)]
         hk = mats[0].shape[1]
@@ -218,6 +239,7 @@ class _GatherQKV(torch.autograd.Function):
         gathered, wq, wk, wv = ctx.saved_tensors
         key, chunk, seq, dim, x_shape = ctx.meta
         ws = workspace(gathered.device, dim)
+        ws._backward_seen = True
         dqkv = dqkv.contiguous()
         mats = [w.reshape(w.shape[0], -1) for w in (wq, wk, wv)]
         hk = mats[0].shape[1]
@@ -239,6 +261,7 @@ class _RowScatter(torch.autograd.Function):
     @staticmethod
     def forward(ctx, o, w, residual2, key, chunk, seq, dim):
         ws = workspace(o.device, dim)
+        key = ws.call_key(key)
         passes = precision.passes()
 
         def launch(c, scatter):
@@ -254,6 +277,7 @@ class _RowScatter(torch.autograd.Function):
         o, w = ctx.saved_tensors
         key, chunk, seq, dim = ctx.meta
         ws = workspace(o.device, dim)
+        ws._backward_seen = True
         dout = dout.contiguous()
         gathered, spec = ws.push_gather(key + ".dG", dout, chunk, seq)
         passes = precision.passes()
@@ -271,6 +295,7 @@ class _SwiGLUTP(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x2, w_gate, w_up, w_down, residual2, key, chunk, seq, dim):
         ws = workspace(x2.device, dim)
+        key = ws.call_key(key)
         passes = precision.passes()
         gathered, spec = ws.push_gather(key + ".G", x2, chunk, seq)
         tokens, hidden = gathered.shape[0], w_gate.shape[1]
@@ -292,6 +317,7 @@ class _SwiGLUTP(torch.autograd.Function):
         gathered, w_gate, w_up, w_down, g, u, h = ctx.saved_tensors
         key, chunk, seq, dim, x_shape = ctx.meta
         ws = workspace(gathered.device, dim)
+        ws._backward_seen = True
         passes = precision.passes()
         dout = dout.contiguous()
         hidden = w_gate.shape[1]

@@ -7,6 +7,7 @@ namespace abacus {
 namespace gemm {
 void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
               int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate, int64_t passes);
+int64_t gemm_n_tiles(int64_t n, int64_t passes);
 int64_t gemm_out_tp(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
                     int64_t b_mode, double alpha, int64_t passes, c10::optional<std::vector<int64_t>> wait,
                     c10::optional<std::vector<int64_t>> scatter);
@@ -80,6 +81,11 @@ void tp_push_rows(torch::Tensor x, std::vector<int64_t> dst_ptrs, std::vector<in
                   int64_t seq, int64_t self, int64_t epoch, torch::Tensor done);
 void tp_reduce_rows(torch::Tensor staging, int64_t world, torch::Tensor counters, int64_t target,
                     c10::optional<torch::Tensor> residual, torch::Tensor out);
+void ep_push_rows(torch::Tensor src, int64_t top_k, torch::Tensor dest_rank, torch::Tensor dest_row,
+                  c10::optional<torch::Tensor> scale, std::vector<int64_t> row_ptrs, std::vector<int64_t> meta_ptrs,
+                  std::vector<int64_t> flag_ptrs, int64_t self, int64_t epoch, torch::Tensor done);
+void ep_combine(torch::Tensor ret, c10::optional<torch::Tensor> weights, int64_t top_k, torch::Tensor counter,
+                int64_t target, torch::Tensor out);
 void ar_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, torch::Tensor counts, bool normalize,
               int64_t rank, int64_t lo, int64_t hi, torch::Tensor exp_avg, torch::Tensor exp_avg_sq, double lr,
               double beta1, double beta2, double eps, double weight_decay, int64_t step);

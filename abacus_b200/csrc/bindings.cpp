@@ -5,6 +5,7 @@
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_out", &abacus::gemm::gemm_out, "tcgen05 tf32 / 3xTF32 GEMM into C");
+  m.def("gemm_n_tiles", &abacus::gemm::gemm_n_tiles, "N tiles of a single-B GEMM of the given output width");
   m.def("gemm_out_tp", &abacus::gemm::gemm_out_tp, "GEMM with a peer-gathered operand and/or row-scattered output");
   m.def("gemm_swiglu_tp", &abacus::gemm::gemm_swiglu_tp, "SwiGLU up-projection over a peer-gathered input");
   m.def("gemm_swiglu_bwd_tp", &abacus::gemm::gemm_swiglu_bwd_tp, "SwiGLU backward GEMM over a peer-gathered dy");
@@ -32,6 +33,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_barrier", &abacus::comm::symm_barrier, "bounded system-scope barrier over peer signal pads");
   m.def("tp_push_rows", &abacus::comm::tp_push_rows, "SP shard -> every rank's gathered buffer + epoch flags");
   m.def("tp_reduce_rows", &abacus::comm::tp_reduce_rows, "sum of scattered partial slots (+ residual) after arrival");
+  m.def("ep_push_rows", &abacus::comm::ep_push_rows, "expert-parallel dispatch: rows into their experts' slabs on peers");
+  m.def("ep_combine", &abacus::comm::ep_combine, "expert-parallel combine: weighted sum of returned rows");
   m.def("ar_adamw", &abacus::comm::ar_adamw, "peer-memory gradient reduce + AdamW + parameter broadcast");
   m.def("read_status", &abacus::host::read_status, "device status word (0 = healthy)");
   m.def("reset_status", &abacus::host::reset_status, "clear the device status word");

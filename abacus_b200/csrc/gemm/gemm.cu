@@ -118,7 +118,9 @@ void apply_comm(Params& p, const Comm& cm, bool a_mn, bool b_mn) {
   if (!cm.wait.empty()) {
     TORCH_CHECK(cm.wait.size() == 6, "wait spec has 6 entries");
     TORCH_CHECK(cm.wait[3] > 0 && cm.wait[4] > 0 && cm.wait[4] % cm.wait[3] == 0, "bad gathered chunking");
-    TORCH_CHECK(cm.wait[1] == 0 || b_mn, "a gathered B operand must store tokens along K (MN-major)");
+    TORCH_CHECK(cm.wait[1] != 1 || b_mn, "a gathered B operand must store tokens along K (MN-major)");
+    TORCH_CHECK(cm.wait[1] >= 0 && cm.wait[1] <= 2, "wait operand: 0 A rows, 1 B rows, 2 all ranks");
+    TORCH_CHECK(cm.wait[1] != 2 || (cm.wait[4] >= 1 && cm.wait[4] <= 8), "all-ranks wait: seq = number of ranks");
     (void)a_mn;
     p.wait_flags = reinterpret_cast<const int*>(cm.wait[0]);
     p.wait_operand = static_cast<int>(cm.wait[1]);
@@ -131,10 +133,16 @@ void apply_comm(Params& p, const Comm& cm, bool a_mn, bool b_mn) {
     TORCH_CHECK(cm.scatter.size() >= 4 && (cm.scatter.size() - 2) % 2 == 0, "bad scatter spec");
     const size_t world = (cm.scatter.size() - 2) / 2;
     TORCH_CHECK(world >= 1 && world <= 8, "scatter over 1..8 ranks");
-    TORCH_CHECK(cm.scatter[0] % BM == 0, "scatter chunk must be a multiple of ", BM, " rows");
-    TORCH_CHECK(cm.scatter[1] == cm.scatter[0] * static_cast<int64_t>(world), "sequence = chunk * ranks");
-    p.scatter_chunk = static_cast<int>(cm.scatter[0]);
-    p.scatter_seq = static_cast<int>(cm.scatter[1]);
+    if (cm.scatter[0] == -1) {
+      // Row-map mode: scatter[1] = device int32 meta per output row.
+      TORCH_CHECK(cm.scatter[1] != 0 && cm.scatter[1] % 4 == 0, "row map pointer");
+      p.scatter_meta = reinterpret_cast<const int*>(cm.scatter[1]);
+    } else {
+      TORCH_CHECK(cm.scatter[0] % BM == 0, "scatter chunk must be a multiple of ", BM, " rows");
+      TORCH_CHECK(cm.scatter[1] == cm.scatter[0] * static_cast<int64_t>(world), "sequence = chunk * ranks");
+      p.scatter_chunk = static_cast<int>(cm.scatter[0]);
+      p.scatter_seq = static_cast<int>(cm.scatter[1]);
+    }
     for (size_t i = 0; i < world; ++i) {
       TORCH_CHECK(cm.scatter[2 + i] % 16 == 0, "scatter destinations must be 16-byte aligned");
       p.scatter_base[i] = reinterpret_cast<float*>(cm.scatter[2 + i]);
@@ -170,10 +178,18 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
   (void)gemm_out_impl(c, a, bs, trans_a, trans_b, b_mode, alpha, residual, accumulate, passes, Comm{});
 }
 
+// Number of N tiles a single-B GEMM of output width n uses (stores per row).
+int64_t gemm_n_tiles(int64_t n, int64_t passes) {
+  check_passes(passes);
+  const int bn = pick_bn(n, static_cast<int>(passes));
+  return (n + bn - 1) / bn;
+}
+
 // gemm_out with the tensor-parallel options: a gathered operand whose rows
 // arrive from peers (wait) and/or an output scattered to the row owners'
 // staging buffers (scatter; no residual / accumulate / split-K then).
-// Returns the output tiles stored on each owner when scattering (0 otherwise).
+// Returns the output tiles stored on each owner when scattering by chunks, the
+// number of N tiles (stores per row) when scattering by row map, else 0.
 int64_t gemm_out_tp(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
                     int64_t b_mode, double alpha, int64_t passes, c10::optional<std::vector<int64_t>> wait,
                     c10::optional<std::vector<int64_t>> scatter) {
@@ -259,6 +275,7 @@ int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tenso
     launch_store(p, dim3(static_cast<unsigned>(tiles), 1), BN, A.mn_major, B[0].mn_major, static_cast<int>(passes),
                  stream);
     if (!scatter) return 0;
+    if (cm.scatter[0] == -1) return p.num_n_tiles;  // each row lands once per N tile
     const int64_t owners = (static_cast<int64_t>(cm.scatter.size()) - 2) / 2;
     TORCH_CHECK(M % (static_cast<int64_t>(BM) * owners) == 0, "scattered rows must split evenly into tiles per owner");
     return (M / BM / owners) * p.num_n_tiles;

@@ -84,6 +84,10 @@ struct alignas(64) Params {
   float* scatter_base[8];
   unsigned* scatter_counter[8];
   int scatter_chunk, scatter_seq;
+  // Row-map scatter (expert parallel combine): with scatter_meta set, output
+  // row r goes to rank meta[r] & 7 at row meta[r] >> 3, and each tile adds to
+  // every destination's counter the number of its rows that went there.
+  const int* scatter_meta;
   int* status;
 };
 
@@ -180,10 +184,19 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     // A, else the K range (MN-major A or B store tokens along K).
     __shared__ int wait_ok;
     if (threadIdx.x == 0) {
-      const bool rows_are_m = p.wait_operand == 0 && !A_MN;
-      const int r0 = rows_are_m ? m0 : kt_begin * BK;
-      const int r1 = rows_are_m ? min(m0 + BM, p.M) : min((kt_begin + num_k) * BK, p.K);
-      wait_ok = wait_gathered_rows(p, r0, r1) ? 1 : 0;
+      if (p.wait_operand == 2) {
+        // Rows pushed by every rank (expert-parallel dispatch): wait for all.
+        bool good = true;
+        for (int r = 0; r < p.wait_seq && good; ++r) {
+          if (r != p.wait_self) good = wait_flag_geq(p.wait_flags + r, p.wait_epoch, p.status);
+        }
+        wait_ok = good ? 1 : 0;
+      } else {
+        const bool rows_are_m = p.wait_operand == 0 && !A_MN;
+        const int r0 = rows_are_m ? m0 : kt_begin * BK;
+        const int r1 = rows_are_m ? min(m0 + BM, p.M) : min((kt_begin + num_k) * BK, p.K);
+        wait_ok = wait_gathered_rows(p, r0, r1) ? 1 : 0;
+      }
     }
     __syncthreads();
     if (!wait_ok) return;
@@ -390,7 +403,10 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
         const int col0 = n0 + c * 32;
         if (row_ok && col0 < p.N) {
           float* crow;
-          if (p.scatter_chunk) {
+          if (p.scatter_meta) {
+            const int meta = p.scatter_meta[row];
+            crow = p.scatter_base[meta & 7] + static_cast<long long>(meta >> 3) * p.ldc + col0;
+          } else if (p.scatter_chunk) {
             const int pos = row % p.scatter_seq;
             const int owner = pos / p.scatter_chunk;
             const long long lrow =
@@ -479,6 +495,25 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
       if (warp == 2 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
         const int owner = (m0 % p.scatter_seq) / p.scatter_chunk;
         red_release_sys_add(p.scatter_counter[owner], 1u);
+      }
+    } else if (EPI == kEpiStore && p.scatter_meta) {
+      // Count this tile's rows per destination rank, then publish them.
+      __shared__ int epi_ok[4];
+      __shared__ unsigned dest_rows[8];
+      if (warp == 2 && lane < 8) dest_rows[lane] = 0u;
+      __threadfence_system();
+      if (lane == 0) epi_ok[q] = ok ? 1 : 0;
+      named_barrier_sync(1, 128);
+      const int dest = row_ok ? (p.scatter_meta[row] & 7) : -1;
+#pragma unroll
+      for (int d = 0; d < 8; ++d) {
+        const unsigned n = __popc(__ballot_sync(0xffffffffu, dest == d));
+        if (lane == 0 && n) atomicAdd(&dest_rows[d], n);
+      }
+      named_barrier_sync(1, 128);
+      if (warp == 2 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
+        for (int d = 0; d < 8; ++d)
+          if (dest_rows[d]) red_release_sys_add(p.scatter_counter[d], dest_rows[d]);
       }
     }
   } else if (PASSES == 3 && warp >= 6) {

@@ -37,7 +37,7 @@ import math
 import torch
 
 from abacus_b200.ops import gemm
-from abacus_b200.parallel import mesh
+from abacus_b200.parallel import ep_fused, mesh, tp_fused
 from abacus_b200.parallel.expert_parallel import (
     _AllToAll,
     _GatherTokenShards,
@@ -285,6 +285,7 @@ class MoEExpertParallel(torch.nn.Module):
         self.w_gate_EDM = torch.nn.Parameter(gate_EDM[start : start + self.local_experts].clone())
         self.w_up_EDM = torch.nn.Parameter(up_EDM[start : start + self.local_experts].clone())
         self.w_down_EMD = torch.nn.Parameter(down_EMD[start : start + self.local_experts].clone())
+        self._ep_key = tp_fused.new_key("moe")
 
     _route = MoE._route
 
@@ -315,6 +316,11 @@ class MoEExpertParallel(torch.nn.Module):
     def _dispatch(self, local_SD, weights_SK, indices_SK):
         """Send each (token, slot) row to the rank owning its expert, run the
         local experts, send results back, weight and sum the K slots."""
+        if ep_fused.usable(local_SD, self.hidden_dim):
+            # Dispatch fused with the permutation, combine fused into the
+            # expert down-projection's epilogue (NVLink peer memory).
+            return ep_fused.dispatch_combine(local_SD, weights_SK, indices_SK, self.w_gate_EDM, self.w_up_EDM,
+                                             self.w_down_EMD, self.n_experts, self._ep_key)
         n_local = local_SD.shape[0]
         flat_ids = indices_SK.reshape(-1)
         flat_weights = weights_SK.reshape(-1)

@@ -55,8 +55,9 @@ def parse_args():
     p.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
     p.add_argument("--seq-len", type=int, default=SEQ_LEN)
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--dp", choices=("fused", "nccl"), default="fused",
-                   help="N>1: fused peer-memory reduce+AdamW kernel, or NCCL bucketed all-reduce + AdamW")
+    p.add_argument("--dp", choices=("fused", "nccl", "zero3"), default="fused",
+                   help="N>1: fused peer-memory reduce+AdamW kernel, NCCL bucketed all-reduce + AdamW, "
+                        "or ZeRO-3 / FSDP (NCCL)")
     return p.parse_args()
 
 
@@ -172,7 +173,10 @@ def build_abacus(args, world, device):
     parallel = None
     if world > 1:
         model = model.to(device)
-        parallel = FusedDataParallel(model) if args.dp == "fused" else DataParallel(model, stage=0)
+        if args.dp == "fused":
+            parallel = FusedDataParallel(model)
+        else:
+            parallel = DataParallel(model, stage=3 if args.dp == "zero3" else 0)
     trainer = Trainer(model, parallel, total_steps=args.warmup + 2 * args.steps + 2)
     return trainer
 
@@ -181,6 +185,9 @@ def build_reference(args, world, device):
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "abacus")):
         return None, "reference not installed in baseline/_ref"
+    if world > 1 and args.dp == "zero3":
+        return None, ("the reference's ZeRO-3 calls dist.all_gather_single / reduce_scatter_single, "
+                      "which torch 2.11 does not provide")
     sys.path.insert(0, ref)
     from abacus.distributed.data_parallel import DataParallel  # noqa: PLC0415
     from abacus.mlp import MLP  # noqa: PLC0415
@@ -282,10 +289,12 @@ def main():
                 "model": "dense GPT ~125M: 12L d768 12x64 heads, SwiGLU 2048, RoPE, QK-norm, vocab 50304",
                 "global_batch": args.global_batch,
                 "seq_len": args.seq_len,
-                "parallelism": f"dp{world}" if world > 1 else "single",
+                "parallelism": (f"zero3-dp{world}" if args.dp == "zero3" else f"dp{world}") if world > 1 else "single",
                 "dp_comm": None if world == 1 else (
                     "fused NVLink peer-memory gradient reduce + AdamW + broadcast kernel"
-                    if impl == "abacus" and args.dp == "fused" else "NCCL all-reduce, then AdamW"),
+                    if impl == "abacus" and args.dp == "fused"
+                    else ("NCCL all-gather / reduce-scatter per unit (ZeRO-3)" if args.dp == "zero3"
+                          else "NCCL all-reduce, then AdamW")),
                 "l2": "inputs/activations larger than L2 (no flush needed)",
                 "compute": "3xTF32 split precision on tcgen05 (fp32 accuracy)" if args.precision == "fp32" and impl == "abacus"
                 else ("tf32 tcgen05" if impl == "abacus" else "reference: torch fp32 (TF32 off)"),

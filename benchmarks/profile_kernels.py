@@ -3,7 +3,13 @@ profiler can capture a few launches of it (used for the summaries in
 profiles/). Inputs exceed the 126 MB L2 where the op is memory-bound; total
 device memory stays under a few GB.
 
-    python benchmarks/profile_kernels.py {gemm3,gemm1,wgrad3,flash_fwd,flash_bwd,rmsnorm,qk,ce,adamw,embedding,all}
+    python benchmarks/profile_kernels.py {gemm3,gemm1,wgrad3,flash_fwd,flash_bwd,rmsnorm,qk,ce,adamw,embedding,
+                                          dense_attn,ar_adamw,tp_push,tp_reduce,all}
+
+The communication families (ar_adamw, tp_push, tp_reduce) run their kernels
+on a one-rank group: the peer tables hold this GPU only, so the figures are
+the kernels' own memory-side cost (NVLink is exercised by the multi-GPU tests
+and benchmarks).
 
 Each family runs twice (warm-up + profiled launch) and prints its device time
 (CUDA events) of the second run.
@@ -99,7 +105,48 @@ def run(name):
         gy = torch.randn_like(y)
         ms = timed(lambda: torch.autograd.grad(emb.embedding(tok, w), w, gy))
         return ms, 3 * y.numel() * 4 / ms / 1e6, "GB/s (fwd+bwd)"
+    if name == "dense_attn":
+        precision.set_precision("fp32")
+        b, l, h, d = 2, 2048, 4, 128
+        q = torch.randn(b * l, h * d, device=dev, requires_grad=True)
+        k = torch.randn(b * l, h * d, device=dev, requires_grad=True)
+        v = torch.randn(b * l, h * d, device=dev, requires_grad=True)
+        ms = timed(lambda: attn.flash_attention(q, k, v, b, h, d))
+        return ms, 4 * b * h * l * l * d / 2 / ms / 1e9, "TFLOP/s (causal, fwd, materialised)"
+    if name in ("ar_adamw", "tp_push", "tp_reduce"):
+        _one_rank_group()
+        if name == "ar_adamw":
+            n = 64 * 1024 * 1024
+            flat = [torch.randn(n, device=dev) for _ in range(2)]
+            m, v = torch.zeros(n, device=dev), torch.zeros(n, device=dev)
+            counts = torch.ones(1, device=dev)
+            ptrs = [[t.data_ptr()] for t in flat]
+            ms = timed(lambda: ext().ar_adamw(ptrs[0], ptrs[1], counts, True, 0, 0, n, m, v, 1e-3, 0.9, 0.999, 1e-8,
+                                              0.01, 1))
+            return ms, 7 * n * 4 / ms / 1e6, "GB/s (grad, param, m, v read; param, m, v written)"
+        from abacus_b200.parallel import tp_fused
+
+        ws = tp_fused.workspace(torch.device(dev), "tp")
+        rows, dim = 32768, 2048
+        x = torch.randn(rows, dim, device=dev)
+        if name == "tp_push":
+            ms = timed(lambda: ws.push_gather("prof.G", x, rows, rows))
+            return ms, 2 * rows * dim * 4 / ms / 1e6, "GB/s (one-rank copy)"
+        staging, _ = ws.buffer("prof.S", rows * dim)
+        counters = torch.full((1,), 1 << 20, dtype=torch.int32, device=dev)
+        out = torch.empty(rows, dim, device=dev)
+        ms = timed(lambda: ext().tp_reduce_rows(staging[: rows * dim], 1, counters, 1, x, out))
+        return ms, 3 * rows * dim * 4 / ms / 1e6, "GB/s (slot + residual read, out written)"
     raise SystemExit(f"unknown kernel family {name}")
+
+
+def _one_rank_group():
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
 
 
 def main():

@@ -124,10 +124,9 @@ __device__ __forceinline__ void split_tile(uint8_t* hi_buf, uint8_t* lo_buf, int
   float4* hi = reinterpret_cast<float4*>(hi_buf);
   float4* lo = reinterpret_cast<float4*>(lo_buf);
   for (int i = tid; i < bytes / 16; i += nthreads) {
+    // hi stays raw (the MMA truncates it to tf32); only lo is written.
     const float4 x = hi[i];
-    const float4 a = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
-    hi[i] = a;
-    lo[i] = make_float4(to_tf32(x.x - a.x), to_tf32(x.y - a.y), to_tf32(x.z - a.z), to_tf32(x.w - a.w));
+    lo[i] = make_float4(tf32_lo_of_raw(x.x), tf32_lo_of_raw(x.y), tf32_lo_of_raw(x.z), tf32_lo_of_raw(x.w));
   }
 }
 

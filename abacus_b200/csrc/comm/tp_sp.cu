@@ -51,11 +51,22 @@ __global__ void __launch_bounds__(256) tp_push_kernel(const __grid_constant__ Pu
       const long long b = r / chunk, i = r % chunk;
       const long long g = b * seq + static_cast<long long>(self) * chunk + i;
       const float4* src = reinterpret_cast<const float4*>(x + r * dim);
-      for (int c = lane; c < d4; c += 32) {
-        const float4 v = src[c];
+      // Four 16-byte loads in flight per lane before the stores.
+      for (int c0 = lane; c0 < d4; c0 += 128) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (c0 + 32 * u < d4) v[u] = __ldg(src + c0 + 32 * u);
+        }
 #pragma unroll
         for (int p = 0; p < kMaxRanks; ++p) {
-          if (p < world) reinterpret_cast<float4*>(a.dst[p] + g * dim)[c] = v;
+          if (p < world) {
+            float4* out = reinterpret_cast<float4*>(a.dst[p] + g * dim);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              if (c0 + 32 * u < d4) out[c0 + 32 * u] = v[u];
+            }
+          }
         }
       }
     }
@@ -127,7 +138,7 @@ void tp_push_rows(torch::Tensor x, std::vector<int64_t> dst_ptrs, std::vector<in
   }
   const long long rows = x.size(0);
   const int sms = at::cuda::getDeviceProperties(x.device().index())->multiProcessorCount;
-  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((rows + 7) / 8, 2LL * sms)));
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((rows + 7) / 8, 4LL * sms)));
   tp_push_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       a, x.data_ptr<float>(), rows, static_cast<int>(x.size(1)), static_cast<int>(chunk), static_cast<int>(seq),
       static_cast<int>(world), static_cast<int>(self), static_cast<int>(epoch), done.data_ptr<int>(),

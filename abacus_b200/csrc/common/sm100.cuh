@@ -325,4 +325,11 @@ __device__ __forceinline__ float to_tf32(float x) {
   return __uint_as_float(r);
 }
 
+// The value a kind::tf32 MMA uses for an fp32 operand element read from shared
+// memory or TMEM: the low 13 mantissa bits dropped (measured on B200). An
+// operand left as raw fp32 therefore acts as its own "hi" part, and only
+// lo = tf32(x - tf32_trunc(x)) must be written beside it.
+__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+__device__ __forceinline__ float tf32_lo_of_raw(float x) { return to_tf32(x - tf32_trunc(x)); }
+
 }  // namespace abacus

@@ -4,9 +4,10 @@
 // * One CTA computes one 128 x BN output tile.
 // * Warp 0: TMA producer. Warp 1: TMEM allocator + single-thread MMA issuer.
 //   Warps 2-5: epilogue (TMEM -> registers -> global). Warps 6-9 (3xTF32
-//   only): split-precision converter that rewrites each landed stage as
-//   hi = tf32(x) in place and lo = tf32(x - hi) beside it, so the MMA warp
-//   can issue lo*hi + hi*lo + hi*hi (fp32-level accuracy on tensor cores).
+//   only): split-precision converter: A rows go to TMEM as hi = tf32(x) and
+//   lo = tf32(x - hi); B stays raw in shared memory (the MMA reads it as its
+//   truncated tf32 hi part) and lo = tf32(x - trunc(x)) is written beside it,
+//   so the MMA warp can issue lo*hi + hi*lo + hi*hi (fp32-level accuracy).
 // * Operands may be K-major (row-major along K; TMA SWIZZLE_128B) or MN-major
 //   (row-major along M/N; TMA SWIZZLE_128B_ATOM_32B, the only MN-major layout
 //   tcgen05 accepts for 32-bit operands). So x@W, dY@W^T and X^T@dY all run
@@ -559,15 +560,15 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
       }
       tmem_st32(lane_addr + Cfg::kATmem + s * 2 * BK, hi);
       tmem_st32(lane_addr + Cfg::kATmem + s * 2 * BK + BK, lo);
-      float4* bsrc = reinterpret_cast<float4*>(stage_b(s));
+      // B stays raw in the landing buffer (the MMA truncates it to its tf32
+      // hi part); only lo is written.
+      const float4* bsrc = reinterpret_cast<const float4*>(stage_b(s));
       float4* bdst = reinterpret_cast<float4*>(stage_blo(s));
       constexpr int kB4 = BN * BK / 4;
 #pragma unroll 4
       for (int i = ct; i < kB4; i += 128) {
         const float4 x = bsrc[i];
-        const float4 h = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
-        bsrc[i] = h;
-        bdst[i] = make_float4(to_tf32(x.x - h.x), to_tf32(x.y - h.y), to_tf32(x.z - h.z), to_tf32(x.w - h.w));
+        bdst[i] = make_float4(tf32_lo_of_raw(x.x), tf32_lo_of_raw(x.y), tf32_lo_of_raw(x.z), tf32_lo_of_raw(x.w));
       }
       tmem_st_wait();
       fence_proxy_async_smem();

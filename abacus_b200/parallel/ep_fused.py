@@ -76,16 +76,26 @@ def _plan(flat_e: torch.Tensor, n_experts: int, local_experts: int, ws):
         "base": base[me].tolist(),
         "recv_max": int(recv_rows.max()),
         "sent_max": int(sent_rows.max()),
+        "typical": int(sent_rows.max()),  # balanced routing: a rank receives what it sends
+        "worst": int(sent_rows.sum()),  # every assignment routed to one rank
         "dest_rank": dest_rank.contiguous(),
         "dest_row": dest_row.contiguous(),
     }
 
 
+def _capacity(needed: int, typical: int, worst: int) -> int:
+    """Rows to allocate for a receive buffer. Every size change is a collective
+    re-allocation, so grow with headroom: twice the balanced load at first,
+    then twice what a step needed, never more than the worst case."""
+    return min(worst, max(needed, 2 * typical, 2 * needed if needed > 2 * typical else 0))
+
+
 def _push(ws, key, src, top_k, plan, scale):
     """Dispatch rows into every rank's buffer `key`; returns (rows, meta, wait spec)."""
     dim = src.shape[1]
-    rows_buf, rows_ptrs = ws.buffer(key, max(1, plan["recv_max"]) * dim)
-    meta_buf, meta_ptrs = ws.buffer(key + ".meta", max(1, plan["recv_max"]))
+    rows_cap = _capacity(plan["recv_max"], plan["typical"], plan["worst"])
+    rows_buf, rows_ptrs = ws.buffer(key, max(1, rows_cap) * dim)
+    meta_buf, meta_ptrs = ws.buffer(key + ".meta", max(1, rows_cap))
     off = ws.slots(key)
     epoch = ws.next_epoch(key)
     done = ws._done.get(key)

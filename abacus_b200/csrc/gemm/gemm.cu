@@ -106,6 +106,20 @@ int pick_splits(long long tiles, int k_tiles, int sms) {
 
 void check_passes(int64_t passes) { TORCH_CHECK(passes == 1 || passes == 3, "passes must be 1 (tf32) or 3 (3xTF32)"); }
 
+// Grid width for `tiles` output tiles: persistent (one CTA per SM, shared
+// with `others` CTAs along y / z) unless the CTAs wait for peer data, which
+// must stay one tile per CTA.
+unsigned tile_grid(Params& p, long long tiles, long long others, int device) {
+  if (p.wait_flags != nullptr || tiles <= 0) {
+    p.persistent = 0;
+    return static_cast<unsigned>(std::max<long long>(tiles, 1));
+  }
+  const int sms = at::cuda::getDeviceProperties(device)->multiProcessorCount;
+  p.persistent = 1;
+  const long long per = std::max<long long>(1, (sms + others - 1) / std::max<long long>(others, 1));
+  return static_cast<unsigned>(std::min(tiles, per));
+}
+
 // Tensor-parallel options of one GEMM launch (see Params in gemm_tcgen05.cuh).
 //   wait    = [flags_ptr, operand (0 A / 1 B), epoch, chunk, seq, self]
 //   scatter = [chunk, seq, base_0..base_{P-1}, counter_0..counter_{P-1}]
@@ -272,7 +286,8 @@ int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tenso
   p.k_tiles_per_split = (k_tiles + splits - 1) / splits;
   splits = (k_tiles + p.k_tiles_per_split - 1) / p.k_tiles_per_split;
   if (splits == 1) {
-    launch_store(p, dim3(static_cast<unsigned>(tiles), 1), BN, A.mn_major, B[0].mn_major, static_cast<int>(passes),
+    const unsigned gx = tile_grid(p, tiles, 1, a.device().index());
+    launch_store(p, dim3(gx, 1), BN, A.mn_major, B[0].mn_major, static_cast<int>(passes),
                  stream);
     if (!scatter) return 0;
     if (cm.scatter[0] == -1) return p.num_n_tiles;  // each row lands once per N tile
@@ -290,7 +305,8 @@ int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tenso
   q.alpha = 1.f;
   q.r = nullptr;
   q.accumulate = 0;
-  launch_store(q, dim3(static_cast<unsigned>(tiles), static_cast<unsigned>(splits)), BN, A.mn_major, B[0].mn_major,
+  const unsigned gxs = tile_grid(q, tiles, splits, a.device().index());
+  launch_store(q, dim3(gxs, static_cast<unsigned>(splits)), BN, A.mn_major, B[0].mn_major,
                static_cast<int>(passes), stream);
   const long long items = M * (N / 4);
   splitk_reduce_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, stream>>>(
@@ -375,7 +391,8 @@ void gemm_batched(torch::Tensor c, torch::Tensor a, torch::Tensor b, bool trans_
   p.status = host::status_ptr(a.device().index());
   p.k_tiles_per_split = static_cast<int>((K + BK - 1) / BK);
   const long long tiles = ((M + BM - 1) / BM) * p.num_n_tiles;
-  launch_store(p, dim3(static_cast<unsigned>(tiles), 1, static_cast<unsigned>(Z)), BN, a_mn, b_mn,
+  const unsigned gxb = tile_grid(p, tiles, Z, a.device().index());
+  launch_store(p, dim3(gxb, 1, static_cast<unsigned>(Z)), BN, a_mn, b_mn,
                static_cast<int>(passes), at::cuda::getCurrentCUDAStream());
 }
 
@@ -425,7 +442,8 @@ void gemm_swiglu_impl(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up,
   p.status = host::status_ptr(x.device().index());
   apply_comm(p, cm, false, true);
   p.k_tiles_per_split = static_cast<int>((A.k + BK - 1) / BK);
-  const int grid = static_cast<int>(((T + BM - 1) / BM) * p.num_n_tiles);
+  const long long tiles = ((T + BM - 1) / BM) * p.num_n_tiles;
+  const unsigned grid = tile_grid(p, tiles, 1, x.device().index());
   auto stream = at::cuda::getCurrentCUDAStream();
   launch_swiglu(p, dim3(grid, 1), BN, static_cast<int>(passes), stream);
 }
@@ -475,7 +493,8 @@ void gemm_swiglu_bwd_impl(torch::Tensor dy, torch::Tensor w_down, torch::Tensor 
   p.status = host::status_ptr(dy.device().index());
   apply_comm(p, cm, false, false);
   p.k_tiles_per_split = static_cast<int>((A.k + BK - 1) / BK);
-  const int grid = static_cast<int>(((T + BM - 1) / BM) * p.num_n_tiles);
+  const long long tiles = ((T + BM - 1) / BM) * p.num_n_tiles;
+  const unsigned grid = tile_grid(p, tiles, 1, dy.device().index());
   auto stream = at::cuda::getCurrentCUDAStream();
   launch_swiglu_bwd(p, dim3(grid, 1), BN, static_cast<int>(passes), stream);
 }

@@ -70,6 +70,9 @@ struct alignas(64) Params {
   //   2: K range [0, m0 + BM)   (P @ V, dS @ K: keys after the last query)
   //   3: K range [m0, K)        (dS^T @ Q, P^T @ dO: queries before the first key)
   int causal;
+  // Persistent schedule: gridDim.x CTAs loop over the tiles (never combined
+  // with the gathered-operand waits below).
+  int persistent;
   // Tensor-parallel all-gather fused into the GEMM: the gathered operand
   // (A when wait_operand == 0, else B) holds rows pushed by the ranks that own
   // them, `wait_chunk` rows per rank inside every `wait_seq`-row sequence. A
@@ -122,7 +125,9 @@ struct Config {
   static constexpr bool kChunked = PASSES == 3;
   static constexpr int kChunk = 2;
   static constexpr int kATmem = 2 * BN;  // first TMEM column of the A stages (3xTF32)
-  static constexpr int kAccCols = kChunked ? 2 * BN + STAGES * 2 * BK : BN;
+  // 1 pass: two accumulator buffers, so a persistent CTA's epilogue of one
+  // tile overlaps the MMAs of the next.
+  static constexpr int kAccCols = kChunked ? 2 * BN + STAGES * 2 * BK : 2 * BN;
   static constexpr uint32_t kTmemCols = kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
 };
 
@@ -136,7 +141,8 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   __shared__ uint64_t full_bar[STAGES];
   __shared__ uint64_t empty_bar[STAGES];
   __shared__ uint64_t conv_bar[STAGES];
-  __shared__ uint64_t accum_bar;
+  __shared__ uint64_t accum_full[2];
+  __shared__ uint64_t accum_empty[2];
   __shared__ uint64_t chunk_full[2];
   __shared__ uint64_t chunk_empty[2];
   __shared__ uint32_t tmem_base_slot;
@@ -157,34 +163,47 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   auto stage_b = [&](int s) { return smem + s * Cfg::kStageBytes + Cfg::kABytes; };
   auto stage_blo = [&](int s) { return smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes; };
 
-  // Tile coordinates, grouped along M for L2 reuse of B.
+  // Tile schedule. A persistent CTA (p.persistent) walks tiles blockIdx.x,
+  // blockIdx.x + gridDim.x, ...; stage, chunk and accumulator phases run on
+  // across tiles, so the epilogue of one tile overlaps the MMAs of the next.
+  // Tiles are grouped along M for L2 reuse of B.
   const int num_m_tiles = (p.M + BM - 1) / BM;
   const int num_n_tiles = p.num_n_tiles;
+  const int total_tiles = num_m_tiles * num_n_tiles;
+  const int tile_step = p.persistent ? static_cast<int>(gridDim.x) : total_tiles;
   constexpr int kGroup = 16;
-  const int tile = blockIdx.x;
-  const int group = tile / (kGroup * num_n_tiles);
-  const int first_m = group * kGroup;
-  const int group_m = min(num_m_tiles - first_m, kGroup);
-  const int in_group = tile - group * kGroup * num_n_tiles;
-  const int m_tile = first_m + in_group % group_m;
-  const int n_tile = in_group / group_m;
-  const int m0 = m_tile * BM;
-  // Output column base. For SwiGLU forward a tile covers BN/2 hidden units.
-  const int n0 = n_tile * (EPI == kEpiSwiGLU ? BN / 2 : BN);
-  if (p.causal == 1 && n0 >= m0 + BM) return;  // fully masked tile (uniform exit)
-  int total_k = (p.K + BK - 1) / BK;
-  int kt_first = 0;
-  if (p.causal == 2) total_k = min(total_k, (m0 + BM + BK - 1) / BK);
-  if (p.causal == 3) kt_first = m0 / BK;
-  const int kt_begin = kt_first + blockIdx.y * p.k_tiles_per_split;
-  const int num_k = max(0, min(total_k, kt_begin + p.k_tiles_per_split) - kt_begin);
+  struct TileInfo {
+    int m0, n0, kt_begin, num_k;
+    bool skip;
+  };
+  auto tile_at = [&](int tile) {
+    TileInfo t;
+    const int group = tile / (kGroup * num_n_tiles);
+    const int first_m = group * kGroup;
+    const int group_m = min(num_m_tiles - first_m, kGroup);
+    const int in_group = tile - group * kGroup * num_n_tiles;
+    t.m0 = (first_m + in_group % group_m) * BM;
+    // Output column base. For SwiGLU forward a tile covers BN/2 hidden units.
+    t.n0 = (in_group / group_m) * (EPI == kEpiSwiGLU ? BN / 2 : BN);
+    t.skip = p.causal == 1 && t.n0 >= t.m0 + BM;  // fully masked tile
+    int total_k = (p.K + BK - 1) / BK;
+    int kt_first = 0;
+    if (p.causal == 2) total_k = min(total_k, (t.m0 + BM + BK - 1) / BK);
+    if (p.causal == 3) kt_first = t.m0 / BK;
+    t.kt_begin = kt_first + static_cast<int>(blockIdx.y) * p.k_tiles_per_split;
+    t.num_k = max(0, min(total_k, t.kt_begin + p.k_tiles_per_split) - t.kt_begin);
+    return t;
+  };
+  if (!p.persistent && tile_at(blockIdx.x).skip) return;  // uniform exit
   const int bz_h = p.batched ? static_cast<int>(blockIdx.z) % p.batch_h : 0;
   const int bz_b = p.batched ? static_cast<int>(blockIdx.z) / p.batch_h : 0;
   if (p.wait_flags != nullptr) {
-    // Rows of the gathered operand this CTA reads: the M range for a K-major
-    // A, else the K range (MN-major A or B store tokens along K).
+    // (Never persistent.) Rows of the gathered operand this CTA reads: the M
+    // range for a K-major A, else the K range (MN-major A or B store tokens
+    // along K).
     __shared__ int wait_ok;
     if (threadIdx.x == 0) {
+      const TileInfo t = tile_at(blockIdx.x);
       if (p.wait_operand == 2) {
         // Rows pushed by every rank (expert-parallel dispatch): wait for all.
         bool good = true;
@@ -194,8 +213,8 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
         wait_ok = good ? 1 : 0;
       } else {
         const bool rows_are_m = p.wait_operand == 0 && !A_MN;
-        const int r0 = rows_are_m ? m0 : kt_begin * BK;
-        const int r1 = rows_are_m ? min(m0 + BM, p.M) : min((kt_begin + num_k) * BK, p.K);
+        const int r0 = rows_are_m ? t.m0 : t.kt_begin * BK;
+        const int r1 = rows_are_m ? min(t.m0 + BM, p.M) : min((t.kt_begin + t.num_k) * BK, p.K);
         wait_ok = wait_gathered_rows(p, r0, r1) ? 1 : 0;
       }
     }
@@ -213,8 +232,9 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
       mbar_init(&empty_bar[s], 1);
       mbar_init(&conv_bar[s], 128);
     }
-    mbar_init(&accum_bar, 1);
     for (int b = 0; b < 2; ++b) {
+      mbar_init(&accum_full[b], 1);
+      mbar_init(&accum_empty[b], 128);
       mbar_init(&chunk_full[b], 1);
       mbar_init(&chunk_empty[b], 128);
     }
@@ -236,55 +256,64 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
-      int issued = 0;
-      for (int kt = 0; kt < num_k; ++kt) {
-        const int s = kt % STAGES;
-        const int use = kt / STAGES;
-        if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
-        const int k0 = (kt_begin + kt) * BK;
-        mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
-        if (A_MN) {
+      int issued = 0;  // k-tiles issued over all tiles of this CTA
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += tile_step) {
+        const TileInfo t = tile_at(tile);
+        if (t.skip) continue;
+        const int m0 = t.m0, n0 = t.n0;
+        for (int kt = 0; kt < t.num_k; ++kt) {
+          const int s = issued % STAGES;
+          const int use = issued / STAGES;
+          if (use > 0 && !mbar_wait(&empty_bar[s], (use - 1) & 1, p.status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          const int k0 = (t.kt_begin + kt) * BK;
+          mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
+          if (A_MN) {
 #pragma unroll
-          for (int c = 0; c < BM / 32; ++c) load(stage_a(s) + c * 32 * BK * 4, &p.tma_a, &full_bar[s], m0 + 32 * c, k0);
-        } else {
-          load(stage_a(s), &p.tma_a, &full_bar[s], k0, m0);
-        }
-        // B source for this (n, k) tile.
-        const CUtensorMap* bmap = &p.tma_b[0];
-        int bn = n0, bk = k0;
-        if (p.b_mode == kBSegN) {
-          const int sidx = n0 / p.seg;
-          bmap = &p.tma_b[sidx];
-          bn = n0 - sidx * p.seg;
-        } else if (p.b_mode == kBSegK) {
-          const int sidx = k0 / p.seg;
-          bmap = &p.tma_b[sidx];
-          bk = k0 - sidx * p.seg;
-        }
-        if (B_MN) {
-          if (p.b_mode == kBDualN) {
-#pragma unroll
-            for (int c = 0; c < BN / 64; ++c) {
-              load(stage_b(s) + c * 32 * BK * 4, &p.tma_b[0], &full_bar[s], n0 + 32 * c, k0);
-              load(stage_b(s) + (c + BN / 64) * 32 * BK * 4, &p.tma_b[1], &full_bar[s], n0 + 32 * c, k0);
+            for (int c = 0; c < BM / 32; ++c) load(stage_a(s) + c * 32 * BK * 4, &p.tma_a, &full_bar[s], m0 + 32 * c, k0);
+          } else {
+            load(stage_a(s), &p.tma_a, &full_bar[s], k0, m0);
+          }
+          // B source for this (n, k) tile.
+          const CUtensorMap* bmap = &p.tma_b[0];
+          int bn = n0, bk = k0;
+          if (p.b_mode == kBSegN) {
+            const int sidx = n0 / p.seg;
+            bmap = &p.tma_b[sidx];
+            bn = n0 - sidx * p.seg;
+          } else if (p.b_mode == kBSegK) {
+            const int sidx = k0 / p.seg;
+            bmap = &p.tma_b[sidx];
+            bk = k0 - sidx * p.seg;
+          }
+          if (B_MN) {
+            if (p.b_mode == kBDualN) {
+  #pragma unroll
+              for (int c = 0; c < BN / 64; ++c) {
+                load(stage_b(s) + c * 32 * BK * 4, &p.tma_b[0], &full_bar[s], n0 + 32 * c, k0);
+                load(stage_b(s) + (c + BN / 64) * 32 * BK * 4, &p.tma_b[1], &full_bar[s], n0 + 32 * c, k0);
+              }
+            } else {
+  #pragma unroll
+              for (int c = 0; c < BN / 32; ++c) load(stage_b(s) + c * 32 * BK * 4, bmap, &full_bar[s], bn + 32 * c, bk);
             }
           } else {
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c) load(stage_b(s) + c * 32 * BK * 4, bmap, &full_bar[s], bn + 32 * c, bk);
+            if (p.b_mode == kBDualN) {
+              load(stage_b(s), &p.tma_b[0], &full_bar[s], k0, n0);
+              load(stage_b(s) + (BN / 2) * BK * 4, &p.tma_b[1], &full_bar[s], k0, n0);
+            } else {
+              load(stage_b(s), bmap, &full_bar[s], bk, bn);
+            }
           }
-        } else {
-          if (p.b_mode == kBDualN) {
-            load(stage_b(s), &p.tma_b[0], &full_bar[s], k0, n0);
-            load(stage_b(s) + (BN / 2) * BK * 4, &p.tma_b[1], &full_bar[s], k0, n0);
-          } else {
-            load(stage_b(s), bmap, &full_bar[s], bk, bn);
-          }
+          ++issued;
         }
-        ++issued;
       }
       // Never leave a bulk copy in flight into a CTA that is about to exit.
-      for (int kt = max(0, issued - STAGES); kt < issued; ++kt) {
-        mbar_wait(&full_bar[kt % STAGES], (kt / STAGES) & 1, nullptr, 0);
+      for (int it = max(0, issued - STAGES); it < issued; ++it) {
+        mbar_wait(&full_bar[it % STAGES], (it / STAGES) & 1, nullptr, 0);
       }
     }
   } else if (warp == 1) {
@@ -292,229 +321,277 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     if (elect_one_sync()) {
       // 3xTF32 reads A from TMEM, which is always K-major (lane = row).
       constexpr uint32_t idesc = idesc_tf32(BM, BN, PASSES == 3 ? false : A_MN, B_MN);
-      bool issued_any = false;
-      for (int kt = 0; kt < num_k; ++kt) {
-        const int s = kt % STAGES;
-        const int use = kt / STAGES;
-        const int chunk = kt / Cfg::kChunk;
-        const int buf = Cfg::kChunked ? (chunk & 1) : 0;
-        const bool first_in_chunk = Cfg::kChunked ? (kt % Cfg::kChunk == 0) : (kt == 0);
-        const bool last_in_chunk = Cfg::kChunked && (kt % Cfg::kChunk == Cfg::kChunk - 1 || kt == num_k - 1);
-        if (Cfg::kChunked && first_in_chunk && chunk >= 2 &&
-            !mbar_wait(&chunk_empty[buf], ((chunk >> 1) - 1) & 1, p.status, kStatusTimeoutAccum))
+      int it = 0;        // k-tiles consumed over all tiles
+      int chunk0 = 0;    // K chunks issued before this tile (3xTF32)
+      int tcount = 0;    // tiles accumulated (1 pass: TMEM buffer = tcount & 1)
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += tile_step) {
+        const TileInfo t = tile_at(tile);
+        if (t.skip) continue;
+        const int num_k = t.num_k;
+        const int abuf = tcount & 1;
+        if (!Cfg::kChunked && tcount >= 2 &&
+            !mbar_wait(&accum_empty[abuf], ((tcount >> 1) - 1) & 1, p.status, kStatusTimeoutAccum)) {
+          ok = false;
           break;
-        uint64_t* ready = PASSES == 3 ? &conv_bar[s] : &full_bar[s];
-        if (!mbar_wait(ready, use & 1, p.status, PASSES == 3 ? kStatusTimeoutConvert : kStatusTimeoutFull)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
-        const uint32_t a_hi = smem_u32(stage_a(s));
-        const uint32_t b_hi = smem_u32(stage_b(s));
-#pragma unroll
-        for (int ks = 0; ks < BK / 8; ++ks) {
-          // One MMA consumes K = 8 tf32 elements (32 bytes).
-          const uint32_t a_off = A_MN ? ks * 8 * 128 : ks * 32;
-          const uint32_t b_off = B_MN ? ks * 8 * 128 : ks * 32;
-          auto desc_a = [&](uint32_t base) {
-            return A_MN ? desc_mnmajor_sw128_32b(base + a_off, 32 * BK * 4) : desc_kmajor_sw128(base + a_off);
-          };
-          auto desc_b = [&](uint32_t base) {
-            return B_MN ? desc_mnmajor_sw128_32b(base + b_off, 32 * BK * 4) : desc_kmajor_sw128(base + b_off);
-          };
-          const uint32_t acc = (first_in_chunk && ks == 0) ? 0u : 1u;
-          if (PASSES == 3) {
-            const uint32_t ta_hi = tmem_base + Cfg::kATmem + s * 2 * BK + ks * 8;
-            const uint32_t ta_lo = ta_hi + BK;
-            const uint32_t b_lo = smem_u32(stage_blo(s));
-            mma_tf32_ts(d_tmem, ta_lo, desc_b(b_hi), idesc, acc);
-            mma_tf32_ts(d_tmem, ta_hi, desc_b(b_lo), idesc, 1u);
-            mma_tf32_ts(d_tmem, ta_hi, desc_b(b_hi), idesc, 1u);
-          } else {
-            mma_tf32_ss(d_tmem, desc_a(a_hi), desc_b(b_hi), idesc, acc);
-          }
         }
-        mma_commit(&empty_bar[s]);
-        if (last_in_chunk) mma_commit(&chunk_full[buf]);
-        issued_any = true;
-      }
-      if (!Cfg::kChunked) {
-        if (issued_any) mma_commit(&accum_bar);
-        else if (num_k == 0) mbar_arrive(&accum_bar);
+        tc_fence_after();
+        bool issued_any = false;
+        for (int kt = 0; kt < num_k; ++kt, ++it) {
+          const int s = it % STAGES;
+          const int use = it / STAGES;
+          const int chunk = chunk0 + kt / Cfg::kChunk;
+          const int buf = Cfg::kChunked ? (chunk & 1) : abuf;
+          const bool first_in_chunk = Cfg::kChunked ? (kt % Cfg::kChunk == 0) : (kt == 0);
+          const bool last_in_chunk = Cfg::kChunked && (kt % Cfg::kChunk == Cfg::kChunk - 1 || kt == num_k - 1);
+          if (Cfg::kChunked && first_in_chunk && chunk >= 2 &&
+              !mbar_wait(&chunk_empty[buf], ((chunk >> 1) - 1) & 1, p.status, kStatusTimeoutAccum)) {
+            ok = false;
+            break;
+          }
+          uint64_t* ready = PASSES == 3 ? &conv_bar[s] : &full_bar[s];
+          if (!mbar_wait(ready, use & 1, p.status, PASSES == 3 ? kStatusTimeoutConvert : kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+          const uint32_t a_hi = smem_u32(stage_a(s));
+          const uint32_t b_hi = smem_u32(stage_b(s));
+  #pragma unroll
+          for (int ks = 0; ks < BK / 8; ++ks) {
+            // One MMA consumes K = 8 tf32 elements (32 bytes).
+            const uint32_t a_off = A_MN ? ks * 8 * 128 : ks * 32;
+            const uint32_t b_off = B_MN ? ks * 8 * 128 : ks * 32;
+            auto desc_a = [&](uint32_t base) {
+              return A_MN ? desc_mnmajor_sw128_32b(base + a_off, 32 * BK * 4) : desc_kmajor_sw128(base + a_off);
+            };
+            auto desc_b = [&](uint32_t base) {
+              return B_MN ? desc_mnmajor_sw128_32b(base + b_off, 32 * BK * 4) : desc_kmajor_sw128(base + b_off);
+            };
+            const uint32_t acc = (first_in_chunk && ks == 0) ? 0u : 1u;
+            if (PASSES == 3) {
+              const uint32_t ta_hi = tmem_base + Cfg::kATmem + s * 2 * BK + ks * 8;
+              const uint32_t ta_lo = ta_hi + BK;
+              const uint32_t b_lo = smem_u32(stage_blo(s));
+              mma_tf32_ts(d_tmem, ta_lo, desc_b(b_hi), idesc, acc);
+              mma_tf32_ts(d_tmem, ta_hi, desc_b(b_lo), idesc, 1u);
+              mma_tf32_ts(d_tmem, ta_hi, desc_b(b_hi), idesc, 1u);
+            } else {
+              mma_tf32_ss(d_tmem, desc_a(a_hi), desc_b(b_hi), idesc, acc);
+            }
+          }
+          mma_commit(&empty_bar[s]);
+          if (last_in_chunk) mma_commit(&chunk_full[buf]);
+          issued_any = true;
+        }
+        if (!ok) break;
+        if (Cfg::kChunked) {
+          chunk0 += (num_k + Cfg::kChunk - 1) / Cfg::kChunk;
+        } else {
+          if (issued_any) mma_commit(&accum_full[abuf]);
+          else mbar_arrive(&accum_full[abuf]);
+          ++tcount;
+        }
       }
       // Every commit must have landed before this CTA's shared memory is
       // released: wait for the last release of each stage (bounded).
-      for (int kt = max(0, num_k - STAGES); kt < num_k && issued_any; ++kt) {
-        if (!mbar_wait(&empty_bar[kt % STAGES], (kt / STAGES) & 1, p.status, kStatusTimeoutEmpty)) break;
+      for (int j = max(0, it - STAGES); j < it; ++j) {
+        if (!mbar_wait(&empty_bar[j % STAGES], (j / STAGES) & 1, p.status, kStatusTimeoutEmpty)) break;
       }
     }
   } else if (warp >= 2 && warp < 6) {
     // ------------------------------------------------------------ epilogue
     const int q = warp % 4;  // TMEM lane quarter this warp may access
-    const int row = m0 + q * 32 + lane;
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    bool ok = num_k > 0;
-    // fp32 (3xTF32) mode: drain each K-chunk accumulator into registers with
-    // round-to-nearest fp32 adds, so the tensor core's own accumulation never
-    // spans more than kChunk k-tiles.
-    float acc[Cfg::kChunked ? BN : 1];
-    if constexpr (Cfg::kChunked) {
-#pragma unroll
-      for (int i = 0; i < BN; ++i) acc[i] = 0.f;
-      const int num_chunks = (num_k + Cfg::kChunk - 1) / Cfg::kChunk;
-      for (int j = 0; j < num_chunks && ok; ++j) {
-        const int buf = j & 1;
-        if (!mbar_wait_warp(&chunk_full[buf], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(taddr + buf * BN + c * 32, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c * 32 + i] += __uint_as_float(v[i]);
-        }
-        tc_fence_before();
-        mbar_arrive(&chunk_empty[buf]);
-      }
-    } else {
-      ok = mbar_wait_warp(&accum_bar, 0, p.status, kStatusTimeoutAccum) && ok;
-      tc_fence_after();
-    }
-    // Fetch the 32 accumulator columns of group c.
-    auto group = [&](int c, float (&out)[32]) {
+    int chunk0 = 0, tcount = 0;
+    bool dead = false;  // a wait ran out: skip all work, keep the named barriers
+    for (int tile = blockIdx.x; tile < total_tiles; tile += tile_step) {
+      const TileInfo t = tile_at(tile);
+      if (t.skip) continue;
+      const int m0 = t.m0, n0 = t.n0, num_k = t.num_k;
+      const int row = m0 + q * 32 + lane;
+      bool ok = num_k > 0 && !dead;
+      const int abuf = tcount & 1;
+      // fp32 (3xTF32) mode: drain each K-chunk accumulator into registers with
+      // round-to-nearest fp32 adds, so the tensor core's own accumulation never
+      // spans more than kChunk k-tiles.
+      float acc[Cfg::kChunked ? BN : 1];
       if constexpr (Cfg::kChunked) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) out[i] = acc[c * 32 + i];
-      } else {
-        uint32_t v[32];
-        tmem_ld32(taddr + c * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) out[i] = __uint_as_float(v[i]);
-      }
-    };
-    const bool row_ok = row < p.M;
-    if (ok && EPI == kEpiStore) {
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        group(c, v);
-        const int col0 = n0 + c * 32;
-        if (row_ok && col0 < p.N) {
-          float* crow;
-          if (p.scatter_meta) {
-            const int meta = p.scatter_meta[row];
-            crow = p.scatter_base[meta & 7] + static_cast<long long>(meta >> 3) * p.ldc + col0;
-          } else if (p.scatter_chunk) {
-            const int pos = row % p.scatter_seq;
-            const int owner = pos / p.scatter_chunk;
-            const long long lrow =
-                static_cast<long long>(row / p.scatter_seq) * p.scatter_chunk + (pos - owner * p.scatter_chunk);
-            crow = p.scatter_base[owner] + lrow * p.ldc + col0;
-          } else {
-            crow = p.c + blockIdx.y * p.split_stride + bz_b * p.c_stride_b + bz_h * p.c_stride_h +
-                   static_cast<long long>(row) * p.ldc + col0;
+        for (int i = 0; i < BN; ++i) acc[i] = 0.f;
+        const int num_chunks = (num_k + Cfg::kChunk - 1) / Cfg::kChunk;
+        for (int j = 0; j < num_chunks && ok; ++j) {
+          const int c_idx = chunk0 + j;
+          const int buf = c_idx & 1;
+          if (!mbar_wait_warp(&chunk_full[buf], (c_idx >> 1) & 1, p.status, kStatusTimeoutAccum)) {
+            ok = false;
+            dead = true;
+            break;
           }
-          const float* rrow = p.r ? p.r + static_cast<long long>(row) * p.ldr + col0 : nullptr;
-          if (col0 + 32 <= p.N) {
+          tc_fence_after();
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 o = make_float4(v[j] * p.alpha, v[j + 1] * p.alpha, v[j + 2] * p.alpha, v[j + 3] * p.alpha);
-              if (rrow) {
-                const float4 rv = *reinterpret_cast<const float4*>(rrow + j);
-                o.x += rv.x; o.y += rv.y; o.z += rv.z; o.w += rv.w;
-              }
-              if (p.accumulate) {
-                const float4 cv = *reinterpret_cast<const float4*>(crow + j);
-                o.x += cv.x; o.y += cv.y; o.z += cv.z; o.w += cv.w;
-              }
-              *reinterpret_cast<float4*>(crow + j) = o;
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(taddr + buf * BN + c * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[c * 32 + i] += __uint_as_float(v[i]);
+          }
+          tc_fence_before();
+          mbar_arrive(&chunk_empty[buf]);
+        }
+        chunk0 += num_chunks;
+      } else {
+        if (!dead) {
+          if (!mbar_wait_warp(&accum_full[abuf], (tcount >> 1) & 1, p.status, kStatusTimeoutAccum)) {
+            ok = false;
+            dead = true;
+          }
+          tc_fence_after();
+        }
+      }
+      // Fetch the 32 accumulator columns of group c.
+      auto group = [&](int c, float (&out)[32]) {
+        if constexpr (Cfg::kChunked) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) out[i] = acc[c * 32 + i];
+        } else {
+          uint32_t v[32];
+          tmem_ld32(taddr + abuf * BN + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) out[i] = __uint_as_float(v[i]);
+        }
+      };
+      const bool row_ok = row < p.M;
+      if (ok && EPI == kEpiStore) {
+  #pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          group(c, v);
+          const int col0 = n0 + c * 32;
+          if (row_ok && col0 < p.N) {
+            float* crow;
+            if (p.scatter_meta) {
+              const int meta = p.scatter_meta[row];
+              crow = p.scatter_base[meta & 7] + static_cast<long long>(meta >> 3) * p.ldc + col0;
+            } else if (p.scatter_chunk) {
+              const int pos = row % p.scatter_seq;
+              const int owner = pos / p.scatter_chunk;
+              const long long lrow =
+                  static_cast<long long>(row / p.scatter_seq) * p.scatter_chunk + (pos - owner * p.scatter_chunk);
+              crow = p.scatter_base[owner] + lrow * p.ldc + col0;
+            } else {
+              crow = p.c + blockIdx.y * p.split_stride + bz_b * p.c_stride_b + bz_h * p.c_stride_h +
+                     static_cast<long long>(row) * p.ldc + col0;
             }
-          } else {
-#pragma unroll
+            const float* rrow = p.r ? p.r + static_cast<long long>(row) * p.ldr + col0 : nullptr;
+            if (col0 + 32 <= p.N) {
+  #pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                float4 o = make_float4(v[j] * p.alpha, v[j + 1] * p.alpha, v[j + 2] * p.alpha, v[j + 3] * p.alpha);
+                if (rrow) {
+                  const float4 rv = *reinterpret_cast<const float4*>(rrow + j);
+                  o.x += rv.x; o.y += rv.y; o.z += rv.z; o.w += rv.w;
+                }
+                if (p.accumulate) {
+                  const float4 cv = *reinterpret_cast<const float4*>(crow + j);
+                  o.x += cv.x; o.y += cv.y; o.z += cv.z; o.w += cv.w;
+                }
+                *reinterpret_cast<float4*>(crow + j) = o;
+              }
+            } else {
+  #pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (col0 + j < p.N) {
+                  float o = v[j] * p.alpha;
+                  if (rrow) o += rrow[j];
+                  if (p.accumulate) o += crow[j];
+                  crow[j] = o;
+                }
+              }
+            }
+          }
+        }
+      } else if (ok && EPI == kEpiSwiGLU) {
+  #pragma unroll
+        for (int c = 0; c < BN / 64; ++c) {
+          float gv[32], uv[32];
+          group(c, gv);
+          group(c + BN / 64, uv);
+          const int col0 = n0 + c * 32;
+          if (row_ok && col0 < p.N) {
+            const long long off = static_cast<long long>(row) * p.ldh + col0;
+  #pragma unroll
             for (int j = 0; j < 32; ++j) {
               if (col0 + j < p.N) {
-                float o = v[j] * p.alpha;
-                if (rrow) o += rrow[j];
-                if (p.accumulate) o += crow[j];
-                crow[j] = o;
+                p.g[off + j] = gv[j];
+                p.u[off + j] = uv[j];
+                p.h[off + j] = silu_f(gv[j]) * uv[j];
+              }
+            }
+          }
+        }
+      } else if (ok && EPI == kEpiSwiGLUBwd) {
+  #pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          group(c, v);
+          const int col0 = n0 + c * 32;
+          if (row_ok && col0 < p.N) {
+            const long long off = static_cast<long long>(row) * p.ld_gu + col0;
+            const long long doff = static_cast<long long>(row) * p.ld_dgu + col0;
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (col0 + j < p.N) {
+                const float dh = v[j];
+                const float g = p.g_in[off + j];
+                const float u = p.u_in[off + j];
+                const float sg = 1.0f / (1.0f + __expf(-g));
+                p.dgu[doff + j] = dh * u * sg * (1.0f + g * (1.0f - sg));
+                p.dgu[doff + p.N + j] = dh * g * sg;
               }
             }
           }
         }
       }
-    } else if (ok && EPI == kEpiSwiGLU) {
-#pragma unroll
-      for (int c = 0; c < BN / 64; ++c) {
-        float gv[32], uv[32];
-        group(c, gv);
-        group(c + BN / 64, uv);
-        const int col0 = n0 + c * 32;
-        if (row_ok && col0 < p.N) {
-          const long long off = static_cast<long long>(row) * p.ldh + col0;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (col0 + j < p.N) {
-              p.g[off + j] = gv[j];
-              p.u[off + j] = uv[j];
-              p.h[off + j] = silu_f(gv[j]) * uv[j];
-            }
-          }
+      if (!Cfg::kChunked) {
+        // The accumulator buffer may take the tile after next.
+        if (!dead) {
+          tc_fence_before();
+          mbar_arrive(&accum_empty[abuf]);
         }
+        ++tcount;
       }
-    } else if (ok && EPI == kEpiSwiGLUBwd) {
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        group(c, v);
-        const int col0 = n0 + c * 32;
-        if (row_ok && col0 < p.N) {
-          const long long off = static_cast<long long>(row) * p.ld_gu + col0;
-          const long long doff = static_cast<long long>(row) * p.ld_dgu + col0;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (col0 + j < p.N) {
-              const float dh = v[j];
-              const float g = p.g_in[off + j];
-              const float u = p.u_in[off + j];
-              const float sg = 1.0f / (1.0f + __expf(-g));
-              p.dgu[doff + j] = dh * u * sg * (1.0f + g * (1.0f - sg));
-              p.dgu[doff + p.N + j] = dh * g * sg;
-            }
-          }
+      if (EPI == kEpiStore && p.scatter_chunk) {
+        // Publish this tile to its owner once all four epilogue warps stored it.
+        __shared__ int epi_ok[4];
+        __threadfence_system();
+        if (lane == 0) epi_ok[q] = ok ? 1 : 0;
+        named_barrier_sync(1, 128);
+        if (warp == 2 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
+          const int owner = (m0 % p.scatter_seq) / p.scatter_chunk;
+          red_release_sys_add(p.scatter_counter[owner], 1u);
         }
-      }
-    }
-    if (EPI == kEpiStore && p.scatter_chunk) {
-      // Publish this tile to its owner once all four epilogue warps stored it.
-      __shared__ int epi_ok[4];
-      __threadfence_system();
-      if (lane == 0) epi_ok[q] = ok ? 1 : 0;
-      named_barrier_sync(1, 128);
-      if (warp == 2 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
-        const int owner = (m0 % p.scatter_seq) / p.scatter_chunk;
-        red_release_sys_add(p.scatter_counter[owner], 1u);
-      }
-    } else if (EPI == kEpiStore && p.scatter_meta) {
-      // Count this tile's rows per destination rank, then publish them.
-      __shared__ int epi_ok[4];
-      __shared__ unsigned dest_rows[8];
-      if (warp == 2 && lane < 8) dest_rows[lane] = 0u;
-      __threadfence_system();
-      if (lane == 0) epi_ok[q] = ok ? 1 : 0;
-      named_barrier_sync(1, 128);
-      const int dest = row_ok ? (p.scatter_meta[row] & 7) : -1;
-#pragma unroll
-      for (int d = 0; d < 8; ++d) {
-        const unsigned n = __popc(__ballot_sync(0xffffffffu, dest == d));
-        if (lane == 0 && n) atomicAdd(&dest_rows[d], n);
-      }
-      named_barrier_sync(1, 128);
-      if (warp == 2 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
-        for (int d = 0; d < 8; ++d)
-          if (dest_rows[d]) red_release_sys_add(p.scatter_counter[d], dest_rows[d]);
+      } else if (EPI == kEpiStore && p.scatter_meta) {
+        // Count this tile's rows per destination rank, then publish them.
+        __shared__ int epi_ok[4];
+        __shared__ unsigned dest_rows[8];
+        if (warp == 2 && lane < 8) dest_rows[lane] = 0u;
+        __threadfence_system();
+        if (lane == 0) epi_ok[q] = ok ? 1 : 0;
+        named_barrier_sync(1, 128);
+        const int dest = row_ok ? (p.scatter_meta[row] & 7) : -1;
+  #pragma unroll
+        for (int d = 0; d < 8; ++d) {
+          const unsigned n = __popc(__ballot_sync(0xffffffffu, dest == d));
+          if (lane == 0 && n) atomicAdd(&dest_rows[d], n);
+        }
+        named_barrier_sync(1, 128);
+        if (warp == 2 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
+          for (int d = 0; d < 8; ++d)
+            if (dest_rows[d]) red_release_sys_add(p.scatter_counter[d], dest_rows[d]);
+        }
       }
     }
   } else if (PASSES == 3 && warp >= 6) {
@@ -522,58 +599,67 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     // Thread = one row of the A tile (its TMEM lane): read the row from the
     // TMA landing buffer (undoing the swizzle), split it into tf32 hi / lo and
     // store both into this stage's TMEM columns. B is split in shared memory:
-    // hi in place, lo beside it.
+    // raw as hi, lo beside it.
     const int ct = threadIdx.x - 192;  // 0..127
     const int row = (warp % 4) * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>((warp % 4) * 32) << 16);
-    for (int kt = 0; kt < num_k; ++kt) {
-      const int s = kt % STAGES;
-      const int use = kt / STAGES;
-      if (!mbar_wait_warp(&full_bar[s], use & 1, p.status, kStatusTimeoutFull)) break;
-      const uint8_t* a = stage_a(s);
-      uint32_t hi[BK], lo[BK];
-      if (A_MN) {
-        // [row / 32][k][128 B], 32-byte granules XOR-swizzled by (k & 3).
-        const uint8_t* base = a + (row / 32) * 32 * BK * 4;
-        const int b = (row % 32) * 4;
-#pragma unroll
-        for (int k = 0; k < BK; ++k) {
-          const int phys = (((b >> 5) ^ (k & 3)) << 5) | (b & 31);
-          const float x = *reinterpret_cast<const float*>(base + k * 128 + phys);
-          const float h = to_tf32(x);
-          hi[k] = __float_as_uint(h);
-          lo[k] = __float_as_uint(to_tf32(x - h));
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += tile_step) {
+      const TileInfo t = tile_at(tile);
+      if (t.skip) continue;
+      for (int kt = 0; kt < t.num_k; ++kt, ++it) {
+        const int s = it % STAGES;
+        const int use = it / STAGES;
+        if (!mbar_wait_warp(&full_bar[s], use & 1, p.status, kStatusTimeoutFull)) {
+          ok = false;
+          break;
         }
-      } else {
-        // Row of 128 bytes, 16-byte chunks XOR-swizzled by (row & 7).
-#pragma unroll
-        for (int c = 0; c < BK / 4; ++c) {
-          const float4 x = *reinterpret_cast<const float4*>(a + row * 128 + ((c ^ (row & 7)) << 4));
-          const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float h = to_tf32(xs[e]);
-            hi[4 * c + e] = __float_as_uint(h);
-            lo[4 * c + e] = __float_as_uint(to_tf32(xs[e] - h));
+          const uint8_t* a = stage_a(s);
+          uint32_t hi[BK], lo[BK];
+          if (A_MN) {
+            // [row / 32][k][128 B], 32-byte granules XOR-swizzled by (k & 3).
+            const uint8_t* base = a + (row / 32) * 32 * BK * 4;
+            const int b = (row % 32) * 4;
+    #pragma unroll
+            for (int k = 0; k < BK; ++k) {
+              const int phys = (((b >> 5) ^ (k & 3)) << 5) | (b & 31);
+              const float x = *reinterpret_cast<const float*>(base + k * 128 + phys);
+              const float h = to_tf32(x);
+              hi[k] = __float_as_uint(h);
+              lo[k] = __float_as_uint(to_tf32(x - h));
+            }
+          } else {
+            // Row of 128 bytes, 16-byte chunks XOR-swizzled by (row & 7).
+    #pragma unroll
+            for (int c = 0; c < BK / 4; ++c) {
+              const float4 x = *reinterpret_cast<const float4*>(a + row * 128 + ((c ^ (row & 7)) << 4));
+              const float xs[4] = {x.x, x.y, x.z, x.w};
+    #pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float h = to_tf32(xs[e]);
+                hi[4 * c + e] = __float_as_uint(h);
+                lo[4 * c + e] = __float_as_uint(to_tf32(xs[e] - h));
+              }
+            }
           }
-        }
+          tmem_st32(lane_addr + Cfg::kATmem + s * 2 * BK, hi);
+          tmem_st32(lane_addr + Cfg::kATmem + s * 2 * BK + BK, lo);
+          // B stays raw in the landing buffer (the MMA truncates it to its tf32
+          // hi part); only lo is written.
+          const float4* bsrc = reinterpret_cast<const float4*>(stage_b(s));
+          float4* bdst = reinterpret_cast<float4*>(stage_blo(s));
+          constexpr int kB4 = BN * BK / 4;
+    #pragma unroll 4
+          for (int i = ct; i < kB4; i += 128) {
+            const float4 x = bsrc[i];
+            bdst[i] = make_float4(tf32_lo_of_raw(x.x), tf32_lo_of_raw(x.y), tf32_lo_of_raw(x.z), tf32_lo_of_raw(x.w));
+          }
+          tmem_st_wait();
+          fence_proxy_async_smem();
+          tc_fence_before();
+        mbar_arrive(&conv_bar[s]);
       }
-      tmem_st32(lane_addr + Cfg::kATmem + s * 2 * BK, hi);
-      tmem_st32(lane_addr + Cfg::kATmem + s * 2 * BK + BK, lo);
-      // B stays raw in the landing buffer (the MMA truncates it to its tf32
-      // hi part); only lo is written.
-      const float4* bsrc = reinterpret_cast<const float4*>(stage_b(s));
-      float4* bdst = reinterpret_cast<float4*>(stage_blo(s));
-      constexpr int kB4 = BN * BK / 4;
-#pragma unroll 4
-      for (int i = ct; i < kB4; i += 128) {
-        const float4 x = bsrc[i];
-        bdst[i] = make_float4(tf32_lo_of_raw(x.x), tf32_lo_of_raw(x.y), tf32_lo_of_raw(x.z), tf32_lo_of_raw(x.w));
-      }
-      tmem_st_wait();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&conv_bar[s]);
     }
   }
 

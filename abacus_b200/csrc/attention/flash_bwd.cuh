@@ -332,6 +332,19 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
       const int entry = block_list[i];
       const int qb = entry & 0xFFFF;
       const bool partial = (entry >> 30) & 1;
+      // This block's lse / Delta / query positions, one query per lane, loaded
+      // before the wait for S^T so their latency hides behind it; the row loop
+      // below broadcasts them with shuffles.
+      float lse_l[NQ / 32], dl_l[NQ / 32];
+      int qpos_l[NQ / 32];
+#pragma unroll
+      for (int c = 0; c < NQ / 32; ++c) {
+        const int qi = qb * NQ + c * 32 + lane;
+        const int qc = min(qi, p.lq - 1);
+        lse_l[c] = __ldg(lse_bh + qc) * kLog2e;
+        dl_l[c] = __ldg(delta_bh + qc);
+        qpos_l[c] = qi < p.lq ? (p.q_pos ? static_cast<int>(__ldg(p.q_pos + qi)) : qi) : INT_MIN;
+      }
       if (!mbar_wait_warp(&st_full, i & 1, p.status, kStatusTimeoutAccum)) {
         ok = false;
         break;
@@ -347,14 +360,10 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
         uint32_t pl[PASSES == 3 ? 32 : 1], dl[PASSES == 3 ? 32 : 1];
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          const int qi = qb * NQ + c * 32 + t;
-          bool valid = true;
-          if (partial) {
-            valid = qi < p.lq && ki < p.lk && (p.q_pos ? static_cast<int>(__ldg(p.q_pos + qi)) : qi) >= kpos;
-          }
-          const int qc = min(qi, p.lq - 1);
-          const float lse2 = __ldg(lse_bh + qc) * kLog2e;
-          const float dl_ = __ldg(delta_bh + qc);
+          const int qpos_t = __shfl_sync(0xffffffffu, qpos_l[c], t);
+          const bool valid = !partial || (ki < p.lk && qpos_t >= kpos);
+          const float lse2 = __shfl_sync(0xffffffffu, lse_l[c], t);
+          const float dl_ = __shfl_sync(0xffffffffu, dl_l[c], t);
           const float pr = valid ? exp2f(__uint_as_float(sv32[t]) * p.scale_log2 - lse2) : 0.f;
           const float ds = pr * (__uint_as_float(dp32[t]) - dl_);
           if (PASSES == 3) {

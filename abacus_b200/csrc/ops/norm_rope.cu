@@ -123,6 +123,45 @@ __global__ void reduce_partials_kernel(const float* __restrict__ partial, float*
   out[j] = s;
 }
 
+// Column sums of a (rows, dim) partial matrix in two deterministic passes:
+// block (column tile of 32, row split) sums its rows with 8 row lanes in a
+// fixed order and combines the lanes in order; then reduce_partials_kernel
+// adds the splits in order. Enough CTAs to keep HBM busy for tall inputs.
+__global__ void __launch_bounds__(256) colsum_split_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                                           long long rows, int dim, long long rows_per_split) {
+  const int lane = threadIdx.x % 32, r0 = threadIdx.x / 32;
+  const int c = blockIdx.x * 32 + lane;
+  const long long begin = static_cast<long long>(blockIdx.y) * rows_per_split;
+  const long long end = min(rows, begin + rows_per_split);
+  float acc = 0.f;
+  if (c < dim) {
+    for (long long r = begin + r0; r < end; r += 8) acc += in[r * dim + c];
+  }
+  __shared__ float sh[8][32];
+  sh[r0][lane] = acc;
+  __syncthreads();
+  if (r0 == 0 && c < dim) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += sh[k][lane];
+    out[static_cast<long long>(blockIdx.y) * dim + c] = t;
+  }
+}
+
+void column_sums(const float* partial, long long rows, int dim, float* out, const torch::TensorOptions& opts,
+                 cudaStream_t s) {
+  const long long splits = std::max<long long>(1, std::min<long long>(1024, (rows + 63) / 64));
+  const long long per = (rows + splits - 1) / splits;
+  auto mid = torch::empty({splits, dim}, opts);
+  dim3 grid(static_cast<unsigned>((dim + 31) / 32), static_cast<unsigned>(splits));
+  colsum_split_kernel<<<grid, 256, 0, s>>>(partial, mid.data_ptr<float>(), rows, dim, per);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
+  reduce_partials_kernel<<<(dim + 255) / 256, 256, 0, s>>>(mid.data_ptr<float>(), out, static_cast<int>(splits), dim);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
+}
+
 // ---------------------------------------------------------------- QK prologue
 // One warp per (token, head). Lane i handles the rotate-half pairs (i, i+K/2),
 // (i+32, i+32+K/2), ... so normalisation and rotation stay in registers.
@@ -324,10 +363,8 @@ void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor gamma, torch::
 #undef LAUNCH
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   abacus::host::note_launch();
-  reduce_partials_kernel<<<(dim + 255) / 256, 256, 0, s>>>(partial.data_ptr<float>(), dgamma.data_ptr<float>(),
-                                                           nblocks * kWarps, dim);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  abacus::host::note_launch();
+  column_sums(partial.data_ptr<float>(), static_cast<long long>(nblocks) * kWarps, dim, dgamma.data_ptr<float>(),
+              x.options(), s);
 }
 
 void qk_prologue_fwd(torch::Tensor qkv, torch::Tensor gq, torch::Tensor gk, torch::Tensor cos_t, torch::Tensor sin_t,
@@ -388,10 +425,8 @@ void qk_prologue_bwd(torch::Tensor qkv, torch::Tensor gq, torch::Tensor gk, torc
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   abacus::host::note_launch();
   auto sums = torch::empty({2 * head_dim}, qkv.options());
-  reduce_partials_kernel<<<static_cast<int>((2 * head_dim + 255) / 256), 256, 0, s>>>(
-      partial.data_ptr<float>(), sums.data_ptr<float>(), nblocks, static_cast<int>(2 * head_dim));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  abacus::host::note_launch();
+  column_sums(partial.data_ptr<float>(), nblocks, static_cast<int>(2 * head_dim), sums.data_ptr<float>(), qkv.options(),
+              s);
   dgq.copy_(sums.narrow(0, 0, head_dim));
   dgk.copy_(sums.narrow(0, head_dim, head_dim));
 }

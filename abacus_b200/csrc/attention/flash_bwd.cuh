@@ -157,7 +157,11 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
   constexpr int NQ = Cfg::kInner;
   static_assert(Cfg::kCols <= 512, "TMEM budget");
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t kv_full, kv_conv, st_full, p_full, part_full, stage_full, stage_conv, stage_empty;
+  // Q / dO tiles come in two groups with their own barriers: the K-major
+  // tiles (S^T, dP^T MMAs) and the MN-major tiles (dV, dK MMAs), so the next
+  // block's K-major tiles load while this block's threads and dV / dK MMAs run.
+  __shared__ uint64_t kv_full, kv_conv, st_full, p_full, part_full;
+  __shared__ uint64_t kf_full, kf_conv, kf_empty, mn_full, mn_conv, mn_empty;
   __shared__ uint32_t tmem_slot;
   __shared__ int n_blocks;
   __shared__ int abort_flag;
@@ -189,9 +193,12 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
     mbar_init(&st_full, 1);
     mbar_init(&p_full, 128);
     mbar_init(&part_full, 1);
-    mbar_init(&stage_full, 1);
-    mbar_init(&stage_conv, 128);
-    mbar_init(&stage_empty, 1);
+    mbar_init(&kf_full, 1);
+    mbar_init(&kf_conv, 128);
+    mbar_init(&kf_empty, 1);
+    mbar_init(&mn_full, 1);
+    mbar_init(&mn_conv, 128);
+    mbar_init(&mn_empty, 1);
     fence_mbar_init();
   }
   if (warp == 0) build_block_list<128, NQ, Cfg::kMaxBlocks>(p, false, k0, block_list, &n_blocks, lane);
@@ -214,22 +221,31 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
         tma_load_2d(sk + c * 128 * 128, &p.tma_k_k, &kv_full, col0 + 32 * c, k_row0);
         tma_load_2d(sv + c * 128 * 128, &p.tma_v_k, &kv_full, col0 + 32 * c, k_row0);
       }
-      int issued = 0;
+      int issued_k = 0, issued_mn = 0;
       for (int i = 0; i < nb; ++i) {
-        if (i >= 1 && !mbar_wait(&stage_empty, (i - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
         const int qrow = q_row_base + (block_list[i] & 0xFFFF) * NQ;
-        mbar_arrive_expect_tx(&stage_full, 4 * Cfg::kQTile);
+        // K-major Q / dO: free once the previous block's S^T / dP^T MMAs ran.
+        if (i >= 1 && !mbar_wait(&kf_empty, (i - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&kf_full, 2 * Cfg::kQTile);
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          tma_load_2d(tile(0, 0) + c * NQ * 128, &p.tma_q_k, &stage_full, col0 + 32 * c, qrow);
-          tma_load_2d(tile(1, 0) + c * NQ * 128, &p.tma_q_mn, &stage_full, col0 + 32 * c, qrow);
-          tma_load_2d(tile(2, 0) + c * NQ * 128, &p.tma_do_k, &stage_full, col0 + 32 * c, qrow);
-          tma_load_2d(tile(3, 0) + c * NQ * 128, &p.tma_do_mn, &stage_full, col0 + 32 * c, qrow);
+          tma_load_2d(tile(0, 0) + c * NQ * 128, &p.tma_q_k, &kf_full, col0 + 32 * c, qrow);
+          tma_load_2d(tile(2, 0) + c * NQ * 128, &p.tma_do_k, &kf_full, col0 + 32 * c, qrow);
         }
-        ++issued;
+        ++issued_k;
+        // MN-major Q / dO: free once the previous block's dV / dK MMAs ran.
+        if (i >= 1 && !mbar_wait(&mn_empty, (i - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&mn_full, 2 * Cfg::kQTile);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          tma_load_2d(tile(1, 0) + c * NQ * 128, &p.tma_q_mn, &mn_full, col0 + 32 * c, qrow);
+          tma_load_2d(tile(3, 0) + c * NQ * 128, &p.tma_do_mn, &mn_full, col0 + 32 * c, qrow);
+        }
+        ++issued_mn;
       }
       mbar_wait(&kv_full, 0, nullptr, 0);
-      if (issued > 0) mbar_wait(&stage_full, (issued - 1) & 1, nullptr, 0);
+      if (issued_k > 0) mbar_wait(&kf_full, (issued_k - 1) & 1, nullptr, 0);
+      if (issued_mn > 0) mbar_wait(&mn_full, (issued_mn - 1) & 1, nullptr, 0);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
@@ -238,7 +254,7 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
       constexpr uint32_t idesc_acc = idesc_tf32(128, D, false, true);
       bool ok = mbar_wait(PASSES == 3 ? &kv_conv : &kv_full, 0, p.status, kStatusTimeoutFull);
       for (int i = 0; i < nb && ok; ++i) {
-        if (!mbar_wait(PASSES == 3 ? &stage_conv : &stage_full, i & 1, p.status, kStatusTimeoutFull)) break;
+        if (!mbar_wait(PASSES == 3 ? &kf_conv : &kf_full, i & 1, p.status, kStatusTimeoutFull)) break;
         tc_fence_after();
         // S^T = K Q^T and dP^T = V dO^T.
 #pragma unroll
@@ -265,7 +281,9 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
           }
         }
         mma_commit(&st_full);
+        mma_commit(&kf_empty);
         if (!mbar_wait(&p_full, i & 1, p.status, kStatusTimeoutAccum)) break;
+        if (!mbar_wait(PASSES == 3 ? &mn_conv : &mn_full, i & 1, p.status, kStatusTimeoutFull)) break;
         tc_fence_after();
         // dV (+)= P^T dO and dK (+)= dS^T Q.
 #pragma unroll
@@ -291,9 +309,12 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
           }
         }
         mma_commit(&part_full);
-        mma_commit(&stage_empty);
+        mma_commit(&mn_empty);
       }
-      if (nb > 0) mbar_wait(&stage_empty, (nb - 1) & 1, p.status, kStatusTimeoutEmpty);
+      if (nb > 0) {
+        mbar_wait(&kf_empty, (nb - 1) & 1, p.status, kStatusTimeoutEmpty);
+        mbar_wait(&mn_empty, (nb - 1) & 1, p.status, kStatusTimeoutEmpty);
+      }
     }
   } else if (warp < 6) {
     // ---------------------------------------------------------------- threads: one key row each
@@ -464,11 +485,16 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
       mbar_arrive(&kv_conv);
     }
     for (int i = 0; i < nb && ok; ++i) {
-      if (!mbar_wait_warp(&stage_full, i & 1, p.status, kStatusTimeoutFull)) break;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) split_tile(tile(w, 0), tile(w, 1), Cfg::kQTile, ct, 128);
+      if (!mbar_wait_warp(&kf_full, i & 1, p.status, kStatusTimeoutFull)) break;
+      split_tile(tile(0, 0), tile(0, 1), Cfg::kQTile, ct, 128);
+      split_tile(tile(2, 0), tile(2, 1), Cfg::kQTile, ct, 128);
       fence_proxy_async_smem();
-      mbar_arrive(&stage_conv);
+      mbar_arrive(&kf_conv);
+      if (!mbar_wait_warp(&mn_full, i & 1, p.status, kStatusTimeoutFull)) break;
+      split_tile(tile(1, 0), tile(1, 1), Cfg::kQTile, ct, 128);
+      split_tile(tile(3, 0), tile(3, 1), Cfg::kQTile, ct, 128);
+      fence_proxy_async_smem();
+      mbar_arrive(&mn_conv);
     }
   }
 
@@ -504,7 +530,10 @@ __global__ void __launch_bounds__(DqCfg<D, PASSES>::kThreads, 1) flash_bwd_dq_ke
   constexpr int NK = Cfg::kInner;
   static_assert(Cfg::kCols <= 512, "TMEM budget");
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t q_full, q_conv, s_full, p_full, dq_full[2], dq_empty[2], stage_full, stage_conv, stage_empty;
+  __shared__ uint64_t q_full, q_conv, s_full, p_full, dq_full[2], dq_empty[2];
+  // K_j / V_j tiles in two groups: K-major K and V (S, dP MMAs) and MN-major K
+  // (dQ MMA), so the next block's K-major tiles load while this block's dQ runs.
+  __shared__ uint64_t kf_full, kf_conv, kf_empty, mn_full, mn_conv, mn_empty;
   __shared__ uint32_t tmem_slot;
   __shared__ int n_blocks;
   __shared__ int abort_flag;
@@ -538,9 +567,12 @@ __global__ void __launch_bounds__(DqCfg<D, PASSES>::kThreads, 1) flash_bwd_dq_ke
       mbar_init(&dq_full[i], 1);
       mbar_init(&dq_empty[i], 128);
     }
-    mbar_init(&stage_full, 1);
-    mbar_init(&stage_conv, 128);
-    mbar_init(&stage_empty, 1);
+    mbar_init(&kf_full, 1);
+    mbar_init(&kf_conv, 128);
+    mbar_init(&kf_empty, 1);
+    mbar_init(&mn_full, 1);
+    mbar_init(&mn_conv, 128);
+    mbar_init(&mn_empty, 1);
     fence_mbar_init();
   }
   if (warp == 0) build_block_list<128, NK, Cfg::kMaxBlocks>(p, true, m0, block_list, &n_blocks, lane);
@@ -562,21 +594,28 @@ __global__ void __launch_bounds__(DqCfg<D, PASSES>::kThreads, 1) flash_bwd_dq_ke
         tma_load_2d(sq + c * 128 * 128, &p.tma_q_k, &q_full, col0 + 32 * c, q_row0);
         tma_load_2d(sdo + c * 128 * 128, &p.tma_do_k, &q_full, col0 + 32 * c, q_row0);
       }
-      int issued = 0;
+      int issued_k = 0, issued_mn = 0;
       for (int j = 0; j < nb; ++j) {
-        if (j >= 1 && !mbar_wait(&stage_empty, (j - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
         const int krow = k_row_base + (block_list[j] & 0xFFFF) * NK;
-        mbar_arrive_expect_tx(&stage_full, 3 * Cfg::kKTile);
+        if (j >= 1 && !mbar_wait(&kf_empty, (j - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&kf_full, 2 * Cfg::kKTile);
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          tma_load_2d(tile(0, 0) + c * NK * 128, &p.tma_k_k, &stage_full, col0 + 32 * c, krow);
-          tma_load_2d(tile(1, 0) + c * NK * 128, &p.tma_k_mn, &stage_full, col0 + 32 * c, krow);
-          tma_load_2d(tile(2, 0) + c * NK * 128, &p.tma_v_k, &stage_full, col0 + 32 * c, krow);
+          tma_load_2d(tile(0, 0) + c * NK * 128, &p.tma_k_k, &kf_full, col0 + 32 * c, krow);
+          tma_load_2d(tile(2, 0) + c * NK * 128, &p.tma_v_k, &kf_full, col0 + 32 * c, krow);
         }
-        ++issued;
+        ++issued_k;
+        if (j >= 1 && !mbar_wait(&mn_empty, (j - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&mn_full, Cfg::kKTile);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          tma_load_2d(tile(1, 0) + c * NK * 128, &p.tma_k_mn, &mn_full, col0 + 32 * c, krow);
+        }
+        ++issued_mn;
       }
       mbar_wait(&q_full, 0, nullptr, 0);
-      if (issued > 0) mbar_wait(&stage_full, (issued - 1) & 1, nullptr, 0);
+      if (issued_k > 0) mbar_wait(&kf_full, (issued_k - 1) & 1, nullptr, 0);
+      if (issued_mn > 0) mbar_wait(&mn_full, (issued_mn - 1) & 1, nullptr, 0);
     }
   } else if (warp == 1) {
     if (elect_one_sync()) {
@@ -584,7 +623,7 @@ __global__ void __launch_bounds__(DqCfg<D, PASSES>::kThreads, 1) flash_bwd_dq_ke
       constexpr uint32_t idesc_dq = idesc_tf32(128, D, false, true);
       bool ok = mbar_wait(PASSES == 3 ? &q_conv : &q_full, 0, p.status, kStatusTimeoutFull);
       for (int j = 0; j < nb && ok; ++j) {
-        if (!mbar_wait(PASSES == 3 ? &stage_conv : &stage_full, j & 1, p.status, kStatusTimeoutFull)) break;
+        if (!mbar_wait(PASSES == 3 ? &kf_conv : &kf_full, j & 1, p.status, kStatusTimeoutFull)) break;
         tc_fence_after();
         // S = Q K^T, dP = dO V^T.
 #pragma unroll
@@ -611,8 +650,10 @@ __global__ void __launch_bounds__(DqCfg<D, PASSES>::kThreads, 1) flash_bwd_dq_ke
           }
         }
         mma_commit(&s_full);
+        mma_commit(&kf_empty);
         const int buf = j & 1;
         if (!mbar_wait(&p_full, j & 1, p.status, kStatusTimeoutAccum)) break;
+        if (!mbar_wait(PASSES == 3 ? &mn_conv : &mn_full, j & 1, p.status, kStatusTimeoutFull)) break;
         if (j >= 2 && !mbar_wait(&dq_empty[buf], ((j >> 1) - 1) & 1, p.status, kStatusTimeoutAccum)) break;
         tc_fence_after();
         // dQ_j = dS K_j.
@@ -634,9 +675,12 @@ __global__ void __launch_bounds__(DqCfg<D, PASSES>::kThreads, 1) flash_bwd_dq_ke
           }
         }
         mma_commit(&dq_full[buf]);
-        mma_commit(&stage_empty);
+        mma_commit(&mn_empty);
       }
-      if (nb > 0) mbar_wait(&stage_empty, (nb - 1) & 1, p.status, kStatusTimeoutEmpty);
+      if (nb > 0) {
+        mbar_wait(&kf_empty, (nb - 1) & 1, p.status, kStatusTimeoutEmpty);
+        mbar_wait(&mn_empty, (nb - 1) & 1, p.status, kStatusTimeoutEmpty);
+      }
     }
   } else if (warp < 6) {
     const int qw = warp % 4;
@@ -725,11 +769,15 @@ __global__ void __launch_bounds__(DqCfg<D, PASSES>::kThreads, 1) flash_bwd_dq_ke
       mbar_arrive(&q_conv);
     }
     for (int j = 0; j < nb && ok; ++j) {
-      if (!mbar_wait_warp(&stage_full, j & 1, p.status, kStatusTimeoutFull)) break;
-#pragma unroll
-      for (int w = 0; w < 3; ++w) split_tile(tile(w, 0), tile(w, 1), Cfg::kKTile, ct, 128);
+      if (!mbar_wait_warp(&kf_full, j & 1, p.status, kStatusTimeoutFull)) break;
+      split_tile(tile(0, 0), tile(0, 1), Cfg::kKTile, ct, 128);
+      split_tile(tile(2, 0), tile(2, 1), Cfg::kKTile, ct, 128);
       fence_proxy_async_smem();
-      mbar_arrive(&stage_conv);
+      mbar_arrive(&kf_conv);
+      if (!mbar_wait_warp(&mn_full, j & 1, p.status, kStatusTimeoutFull)) break;
+      split_tile(tile(1, 0), tile(1, 1), Cfg::kKTile, ct, 128);
+      fence_proxy_async_smem();
+      mbar_arrive(&mn_conv);
     }
   }
 

@@ -95,29 +95,38 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, l
 }
 
 // Number of K splits for a GEMM with `tiles` output tiles and `k_tiles`
-// 32-deep k-tiles: enough CTAs for two waves, at least 32 k-tiles per split.
+// 32-deep k-tiles. Work units (tile, split) are shared evenly by one
+// persistent CTA per SM, so pick the split count whose busiest SM does the
+// fewest k-tiles, with at least 16 k-tiles per split; ties go to fewer splits
+// (less reduction traffic).
 int pick_splits(long long tiles, int k_tiles, int sms) {
   if (tiles >= 2LL * sms || k_tiles < 64) return 1;
-  long long s = (2LL * sms + tiles - 1) / tiles;
-  s = std::min<long long>(s, 16);
-  s = std::min<long long>(s, k_tiles / 32);
-  return static_cast<int>(std::max<long long>(s, 1));
+  long long best_s = 1, best_cost = -1;
+  for (long long s = 1; s <= 16 && k_tiles / s >= 16; ++s) {
+    const long long per_unit = (k_tiles + s - 1) / s;
+    const long long rounds = (tiles * s + sms - 1) / sms;
+    const long long cost = rounds * per_unit;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_s = s;
+    }
+  }
+  return static_cast<int>(best_s);
 }
 
 void check_passes(int64_t passes) { TORCH_CHECK(passes == 1 || passes == 3, "passes must be 1 (tf32) or 3 (3xTF32)"); }
 
-// Grid width for `tiles` output tiles: persistent (one CTA per SM, shared
-// with `others` CTAs along y / z) unless the CTAs wait for peer data, which
-// must stay one tile per CTA.
-unsigned tile_grid(Params& p, long long tiles, long long others, int device) {
-  if (p.wait_flags != nullptr || tiles <= 0) {
+// Grid width for `units` work units (tiles x splits x batched matrices):
+// persistent (one CTA per SM) unless the CTAs wait for peer data, which must
+// stay one unit per CTA.
+unsigned tile_grid(Params& p, long long units, int device) {
+  if (p.wait_flags != nullptr || units <= 0) {
     p.persistent = 0;
-    return static_cast<unsigned>(std::max<long long>(tiles, 1));
+    return static_cast<unsigned>(std::max<long long>(units, 1));
   }
   const int sms = at::cuda::getDeviceProperties(device)->multiProcessorCount;
   p.persistent = 1;
-  const long long per = std::max<long long>(1, (sms + others - 1) / std::max<long long>(others, 1));
-  return static_cast<unsigned>(std::min(tiles, per));
+  return static_cast<unsigned>(std::min<long long>(units, sms));
 }
 
 // Tensor-parallel options of one GEMM launch (see Params in gemm_tcgen05.cuh).
@@ -286,7 +295,9 @@ int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tenso
   p.k_tiles_per_split = (k_tiles + splits - 1) / splits;
   splits = (k_tiles + p.k_tiles_per_split - 1) / p.k_tiles_per_split;
   if (splits == 1) {
-    const unsigned gx = tile_grid(p, tiles, 1, a.device().index());
+    p.splits = 1;
+    p.batch_z = 1;
+    const unsigned gx = tile_grid(p, tiles, a.device().index());
     launch_store(p, dim3(gx, 1), BN, A.mn_major, B[0].mn_major, static_cast<int>(passes),
                  stream);
     if (!scatter) return 0;
@@ -305,8 +316,10 @@ int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tenso
   q.alpha = 1.f;
   q.r = nullptr;
   q.accumulate = 0;
-  const unsigned gxs = tile_grid(q, tiles, splits, a.device().index());
-  launch_store(q, dim3(gxs, static_cast<unsigned>(splits)), BN, A.mn_major, B[0].mn_major,
+  q.splits = splits;
+  q.batch_z = 1;
+  const unsigned gxs = tile_grid(q, tiles * splits, a.device().index());
+  launch_store(q, dim3(gxs, 1), BN, A.mn_major, B[0].mn_major,
                static_cast<int>(passes), stream);
   const long long items = M * (N / 4);
   splitk_reduce_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, stream>>>(
@@ -391,8 +404,10 @@ void gemm_batched(torch::Tensor c, torch::Tensor a, torch::Tensor b, bool trans_
   p.status = host::status_ptr(a.device().index());
   p.k_tiles_per_split = static_cast<int>((K + BK - 1) / BK);
   const long long tiles = ((M + BM - 1) / BM) * p.num_n_tiles;
-  const unsigned gxb = tile_grid(p, tiles, Z, a.device().index());
-  launch_store(p, dim3(gxb, 1, static_cast<unsigned>(Z)), BN, a_mn, b_mn,
+  p.splits = 1;
+  p.batch_z = static_cast<int>(Z);
+  const unsigned gxb = tile_grid(p, tiles * Z, a.device().index());
+  launch_store(p, dim3(gxb, 1, 1), BN, a_mn, b_mn,
                static_cast<int>(passes), at::cuda::getCurrentCUDAStream());
 }
 
@@ -443,7 +458,9 @@ void gemm_swiglu_impl(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up,
   apply_comm(p, cm, false, true);
   p.k_tiles_per_split = static_cast<int>((A.k + BK - 1) / BK);
   const long long tiles = ((T + BM - 1) / BM) * p.num_n_tiles;
-  const unsigned grid = tile_grid(p, tiles, 1, x.device().index());
+  p.splits = 1;
+  p.batch_z = 1;
+  const unsigned grid = tile_grid(p, tiles, x.device().index());
   auto stream = at::cuda::getCurrentCUDAStream();
   launch_swiglu(p, dim3(grid, 1), BN, static_cast<int>(passes), stream);
 }
@@ -494,7 +511,9 @@ void gemm_swiglu_bwd_impl(torch::Tensor dy, torch::Tensor w_down, torch::Tensor 
   apply_comm(p, cm, false, false);
   p.k_tiles_per_split = static_cast<int>((A.k + BK - 1) / BK);
   const long long tiles = ((T + BM - 1) / BM) * p.num_n_tiles;
-  const unsigned grid = tile_grid(p, tiles, 1, dy.device().index());
+  p.splits = 1;
+  p.batch_z = 1;
+  const unsigned grid = tile_grid(p, tiles, dy.device().index());
   auto stream = at::cuda::getCurrentCUDAStream();
   launch_swiglu_bwd(p, dim3(grid, 1), BN, static_cast<int>(passes), stream);
 }

@@ -45,7 +45,7 @@ struct alignas(64) Params {
   const float* r;    // residual added by the store epilogue (nullable)
   long long ldr;
   int accumulate;    // store epilogue: C += result
-  // Split-K: CTA (tile, blockIdx.y) covers k-tiles [y * k_tiles_per_split, ...)
+  // Split-K: work unit (tile, split y) covers k-tiles [y * k_tiles_per_split, ...)
   // and stores its fp32 partial at c + y * split_stride (reduced afterwards).
   int k_tiles_per_split;
   long long split_stride;
@@ -73,6 +73,10 @@ struct alignas(64) Params {
   // Persistent schedule: gridDim.x CTAs loop over the tiles (never combined
   // with the gathered-operand waits below).
   int persistent;
+  // Work units = tiles x splits x batch_z (split-K and batched matrices are
+  // flattened into the persistent schedule, so every SM gets an equal share).
+  int splits;
+  int batch_z;
   // Tensor-parallel all-gather fused into the GEMM: the gathered operand
   // (A when wait_operand == 0, else B) holds rows pushed by the ranks that own
   // them, `wait_chunk` rows per rank inside every `wait_seq`-row sequence. A
@@ -170,14 +174,24 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   const int num_m_tiles = (p.M + BM - 1) / BM;
   const int num_n_tiles = p.num_n_tiles;
   const int total_tiles = num_m_tiles * num_n_tiles;
-  const int tile_step = p.persistent ? static_cast<int>(gridDim.x) : total_tiles;
+  const int n_splits = max(1, p.splits);
+  const int n_z = max(1, p.batch_z);
+  const int total_units = total_tiles * n_splits * n_z;
+  const int unit_step = p.persistent ? static_cast<int>(gridDim.x) : total_units;
   constexpr int kGroup = 16;
   struct TileInfo {
     int m0, n0, kt_begin, num_k;
+    int split, zh, zb;
     bool skip;
   };
-  auto tile_at = [&](int tile) {
+  auto tile_at = [&](int unit) {
     TileInfo t;
+    const int tile = unit % total_tiles;
+    const int rest = unit / total_tiles;
+    t.split = rest % n_splits;
+    const int z = rest / n_splits;
+    t.zh = p.batched ? z % p.batch_h : 0;
+    t.zb = p.batched ? z / p.batch_h : 0;
     const int group = tile / (kGroup * num_n_tiles);
     const int first_m = group * kGroup;
     const int group_m = min(num_m_tiles - first_m, kGroup);
@@ -190,13 +204,12 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     int kt_first = 0;
     if (p.causal == 2) total_k = min(total_k, (t.m0 + BM + BK - 1) / BK);
     if (p.causal == 3) kt_first = t.m0 / BK;
-    t.kt_begin = kt_first + static_cast<int>(blockIdx.y) * p.k_tiles_per_split;
+    t.kt_begin = kt_first + t.split * p.k_tiles_per_split;
     t.num_k = max(0, min(total_k, t.kt_begin + p.k_tiles_per_split) - t.kt_begin);
     return t;
   };
   if (!p.persistent && tile_at(blockIdx.x).skip) return;  // uniform exit
-  const int bz_h = p.batched ? static_cast<int>(blockIdx.z) % p.batch_h : 0;
-  const int bz_b = p.batched ? static_cast<int>(blockIdx.z) / p.batch_h : 0;
+  int cur_h = 0, cur_b = 0;  // batched matrix of the tile being loaded (producer)
   if (p.wait_flags != nullptr) {
     // (Never persistent.) Rows of the gathered operand this CTA reads: the M
     // range for a K-major A, else the K range (MN-major A or B store tokens
@@ -222,7 +235,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     if (!wait_ok) return;
   }
   auto load = [&](void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-    if (p.batched) tma_load_4d(dst, map, bar, x, y, bz_h, bz_b);
+    if (p.batched) tma_load_4d(dst, map, bar, x, y, cur_h, cur_b);
     else tma_load_2d(dst, map, bar, x, y);
   };
 
@@ -258,10 +271,12 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     if (elect_one_sync()) {
       int issued = 0;  // k-tiles issued over all tiles of this CTA
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += tile_step) {
+      for (int tile = blockIdx.x; tile < total_units && ok; tile += unit_step) {
         const TileInfo t = tile_at(tile);
         if (t.skip) continue;
         const int m0 = t.m0, n0 = t.n0;
+        cur_h = t.zh;
+        cur_b = t.zb;
         for (int kt = 0; kt < t.num_k; ++kt) {
           const int s = issued % STAGES;
           const int use = issued / STAGES;
@@ -325,7 +340,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
       int chunk0 = 0;    // K chunks issued before this tile (3xTF32)
       int tcount = 0;    // tiles accumulated (1 pass: TMEM buffer = tcount & 1)
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += tile_step) {
+      for (int tile = blockIdx.x; tile < total_units && ok; tile += unit_step) {
         const TileInfo t = tile_at(tile);
         if (t.skip) continue;
         const int num_k = t.num_k;
@@ -405,7 +420,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     int chunk0 = 0, tcount = 0;
     bool dead = false;  // a wait ran out: skip all work, keep the named barriers
-    for (int tile = blockIdx.x; tile < total_tiles; tile += tile_step) {
+    for (int tile = blockIdx.x; tile < total_units; tile += unit_step) {
       const TileInfo t = tile_at(tile);
       if (t.skip) continue;
       const int m0 = t.m0, n0 = t.n0, num_k = t.num_k;
@@ -482,7 +497,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
                   static_cast<long long>(row / p.scatter_seq) * p.scatter_chunk + (pos - owner * p.scatter_chunk);
               crow = p.scatter_base[owner] + lrow * p.ldc + col0;
             } else {
-              crow = p.c + blockIdx.y * p.split_stride + bz_b * p.c_stride_b + bz_h * p.c_stride_h +
+              crow = p.c + t.split * p.split_stride + t.zb * p.c_stride_b + t.zh * p.c_stride_h +
                      static_cast<long long>(row) * p.ldc + col0;
             }
             const float* rrow = p.r ? p.r + static_cast<long long>(row) * p.ldr + col0 : nullptr;
@@ -605,7 +620,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>((warp % 4) * 32) << 16);
     int it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += tile_step) {
+    for (int tile = blockIdx.x; tile < total_units && ok; tile += unit_step) {
       const TileInfo t = tile_at(tile);
       if (t.skip) continue;
       for (int kt = 0; kt < t.num_k; ++kt, ++it) {

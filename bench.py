@@ -3,8 +3,10 @@
 Model: 12 layers, d_model 768, 12 heads x 64, SwiGLU hidden 2048, RoPE,
 QK-norm, vocab 50304, untied embeddings, fp32 parameters. Data: synthetic
 uniform-random int64 tokens (seed 0), seq_len 1024, global batch 64
-sequences (64 / N per rank; strong scaling). Data parallel (DDP, ZeRO-0) for
-N > 1, one process per GPU over NCCL.
+sequences (64 / N per rank; strong scaling). Data parallel for N > 1, one
+process per GPU: by default the fused peer-memory gradient reduce + AdamW +
+parameter broadcast kernel (``--dp fused``); ``--dp nccl`` runs bucketed NCCL
+all-reduce + AdamW and ``--dp zero3`` ZeRO-3 on NCCL.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl abacus|reference]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...

@@ -61,6 +61,7 @@ void flash_attn_bwd_cp(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
                        int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
                        c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes,
                        std::vector<int64_t> scatter);
+void flash_fwd_trace(c10::optional<torch::Tensor> buf);
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                     int64_t batch, int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes);

@@ -45,6 +45,9 @@ void launch_fwd(const FwdParams& p, dim3 grid, cudaStream_t s) {
   abacus::host::note_launch();
 }
 
+// Optional phase trace of the forward kernel (debugging / profiling aid).
+long long* g_fwd_trace = nullptr;
+
 const int64_t* positions_ptr(const c10::optional<torch::Tensor>& pos, int64_t len, const char* name) {
   if (!pos) return nullptr;
   TORCH_CHECK(pos->is_cuda() && pos->scalar_type() == torch::kInt64 && pos->is_contiguous() && pos->numel() == len,
@@ -65,6 +68,18 @@ void flash_bwd_impl(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos, int64_t passes,
                     const std::vector<int64_t>& scatter);
 }  // namespace
+
+// Point the forward kernel's phase trace at `buf` (>= 9 * 64 int64 on the
+// device), or switch it off with None.
+void flash_fwd_trace(c10::optional<torch::Tensor> buf) {
+  if (!buf) {
+    g_fwd_trace = nullptr;
+    return;
+  }
+  TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == torch::kInt64 && buf->is_contiguous() && buf->numel() >= 9 * 64,
+              "trace buffer: contiguous int64 CUDA tensor of >= 576 entries");
+  g_fwd_trace = reinterpret_cast<long long*>(buf->data_ptr<int64_t>());
+}
 
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                     int64_t batch, int64_t heads, int64_t head_dim, int64_t lq, int64_t lk, double scale,
@@ -116,6 +131,7 @@ void flash_fwd_impl(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
   p.lk = static_cast<int>(lk);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.status = host::status_ptr(q.device().index());
+  p.trace = g_fwd_trace;
   if (!wait.empty()) {
     TORCH_CHECK(wait[2] >= 1 && wait[2] <= 8 && wait[3] >= 0 && wait[3] < wait[2], "bad wait spec");
     p.wait_flags = reinterpret_cast<const int*>(wait[0]);

@@ -51,6 +51,10 @@ struct FwdParams {
   const int* wait_flags;
   int wait_epoch, wait_world, wait_self;
   int* status;
+  // Optional phase trace (clock64 stamps of CTA (0, 0, 0), slot * 64 + block):
+  // 0 K/V load issued, 1 K/V split, 2 S issued, 3 PV issued, 4 S seen by the
+  // softmax, 5 P written, 6 PV seen, 7 PV folded, 8 (+0 start, +1 set-up, +2 end).
+  long long* trace;
 };
 
 template <int D, int PASSES>
@@ -86,6 +90,10 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
   __shared__ int block_list[Cfg::kMaxBlocks];  // key block index | (needs_mask << 30)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const bool traced = p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+#define ABACUS_FWD_TRACE(slot, j) \
+  if (traced && (j) < 64) p.trace[(slot) * 64 + (j)] = clock64();
+  if (threadIdx.x == 0) ABACUS_FWD_TRACE(8, 0)
   // Abort early (uniformly for the whole CTA) if an earlier kernel on this
   // device already recorded an error.
   __shared__ int abort_flag;
@@ -189,6 +197,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   const int nb = n_blocks;
+  if (threadIdx.x == 0) ABACUS_FWD_TRACE(8, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
@@ -205,6 +214,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
         if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
         const int kb = block_list[j] & 0xFFFF;
         const int krow = k_row0 + kb * kBlockN;
+        ABACUS_FWD_TRACE(0, j)
         mbar_arrive_expect_tx(&kv_full[s], Cfg::kKBytes + Cfg::kVBytes);
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -227,6 +237,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
         const int s = j & 1;
         if (!mbar_wait(PASSES == 3 ? &kv_conv[s] : &kv_full[s], (j >> 1) & 1, p.status, kStatusTimeoutFull))
           return false;
+        ABACUS_FWD_TRACE(2, j)
         tc_fence_after();
         const uint32_t d = tmem + s * Cfg::kSPCols;
 #pragma unroll
@@ -255,6 +266,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
         const int s = j & 1;
         if (!mbar_wait(&p_full[s], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) return false;
         if (j >= 2 && !mbar_wait(&pv_empty[s], ((j >> 1) - 1) & 1, p.status, kStatusTimeoutAccum)) return false;
+        ABACUS_FWD_TRACE(3, j)
         tc_fence_after();
         const uint32_t d = tmem + Cfg::kPVBase + s * D;
         const uint32_t p_hi = tmem + s * Cfg::kSPCols;
@@ -309,6 +321,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
           ok = false;
           break;
         }
+        if (threadIdx.x == 64) ABACUS_FWD_TRACE(4, j)
         tc_fence_after();
         // Scaled, masked scores of 32 columns of S_j (re-read from TMEM, which
         // is cheaper than keeping 64 scores live in registers).
@@ -365,6 +378,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&p_full[s]);
+        if (threadIdx.x == 64) ABACUS_FWD_TRACE(5, j)
       }
       if (j >= 1) {
         // Fold PV_{j-1}: o = o * alpha_{j-1} + PV_{j-1}.
@@ -373,6 +387,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
           ok = false;
           break;
         }
+        if (threadIdx.x == 64) ABACUS_FWD_TRACE(6, j - 1)
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -384,6 +399,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
         }
         tc_fence_before();
         mbar_arrive(&pv_empty[s]);
+        if (threadIdx.x == 64) ABACUS_FWD_TRACE(7, j - 1)
       }
       alpha_prev = alpha;
     }
@@ -421,11 +437,14 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
       split(v_hi(s), v_lo(s), Cfg::kVBytes);
       fence_proxy_async_smem();
       mbar_arrive(&kv_conv[s]);
+      if (ct == 0) ABACUS_FWD_TRACE(1, j)
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) ABACUS_FWD_TRACE(8, 2)
+#undef ABACUS_FWD_TRACE
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);

@@ -26,6 +26,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_fwd_cp", &abacus::attn::flash_attn_fwd_cp, "flash forward over peer-pushed K/V (context parallel)");
   m.def("flash_attn_bwd_cp", &abacus::attn::flash_attn_bwd_cp, "flash backward scattering dK/dV to their owners");
   m.def("flash_attn_fwd", &abacus::attn::flash_attn_fwd);
+  m.def("flash_fwd_trace", &abacus::attn::flash_fwd_trace, "phase trace of the flash forward (debugging)");
   m.def("flash_attn_bwd", &abacus::attn::flash_attn_bwd);
   m.def("launch_count", &abacus::host::launch_count, "number of abacus kernels launched by this process");
   m.def("wait_flag", &abacus::comm::wait_flag, "bounded device wait for a flag (error status on timeout)");

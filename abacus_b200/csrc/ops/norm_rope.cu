@@ -11,6 +11,8 @@
 #include "../api.h"
 #include "rmsnorm_noalloc.h"
 #include <algorithm>
+#include <atomic>
+#include <cstdint>
 #include <mutex>
 #include "../common/host.h"
 
@@ -446,18 +448,24 @@ namespace abacus {
 namespace ops {
 namespace {
 
-// Scratch for the dgamma partial rows: (blocks * kWarps) rows of `dim` floats.
+// Scratch for the dgamma reduction, split in two regions: per-warp partial
+// rows ((blocks * kWarps) rows of `dim` floats) and the per-split column sums
+// of those rows (`splits` rows of `dim` floats).
 constexpr long long kNoAllocScratchFloats = 1LL << 20;  // 4 MiB per GPU
+constexpr long long kNoAllocMidFloats = 1LL << 18;      // last 1 MiB: split sums
+constexpr long long kNoAllocPartialFloats = kNoAllocScratchFloats - kNoAllocMidFloats;
 static __device__ __align__(256) float g_rmsnorm_noalloc_scratch[kNoAllocScratchFloats];
 
-// Device address of the scratch array, looked up once per device.
-float* g_scratch_addr[64] = {nullptr};
-int g_sm_count[64] = {0};
+// Per device: SM count, then the scratch array's device address. The address
+// is published last with release order, so a reader that sees it (acquire)
+// also sees the SM count.
+std::atomic<float*> g_scratch_addr[64] = {};
+std::atomic<int> g_sm_count[64] = {};
 std::mutex g_noalloc_mu;
 
 int noalloc_setup(int device) {
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_scratch_addr[device] != nullptr) return 0;
+  if (g_scratch_addr[device].load(std::memory_order_acquire) != nullptr) return 0;
   // Host code cannot use the array's name as a device address: ask the
   // runtime for it, with `device` current.
   void* ptr = nullptr;
@@ -466,10 +474,12 @@ int noalloc_setup(int device) {
   int sms = 0;
   err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (err != cudaSuccess) return static_cast<int>(err);
-  g_sm_count[device] = sms;
-  g_scratch_addr[device] = static_cast<float*>(ptr);
+  g_sm_count[device].store(sms, std::memory_order_relaxed);
+  g_scratch_addr[device].store(static_cast<float*>(ptr), std::memory_order_release);
   return 0;
 }
+
+bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
 
 }  // namespace
 }  // namespace ops
@@ -482,27 +492,36 @@ extern "C" __attribute__((visibility("default"))) int abacus_rmsnorm_bwd_noalloc
   if (rows < 0 || dim <= 0 || dim % 4 != 0 || dim > 4096) return ABACUS_NOALLOC_EBADSIZE;
   if (dy == nullptr || x == nullptr || gamma == nullptr || rstd == nullptr || dx == nullptr || dgamma == nullptr)
     return ABACUS_NOALLOC_EBADSIZE;
+  // The kernels move dy / x / dx / gamma / dgamma / scratch rows as float4.
+  if (misaligned16(dy) || misaligned16(x) || misaligned16(gamma) || misaligned16(rstd) || misaligned16(dx) ||
+      misaligned16(dgamma))
+    return ABACUS_NOALLOC_EBADSIZE;
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return static_cast<int>(err);
   if (device < 0 || device >= 64) return ABACUS_NOALLOC_EBADSIZE;
-  if (g_scratch_addr[device] == nullptr) {
+  float* scratch = g_scratch_addr[device].load(std::memory_order_acquire);
+  if (scratch == nullptr) {
     const int rc = noalloc_setup(device);
     if (rc != 0) return rc;
+    scratch = g_scratch_addr[device].load(std::memory_order_acquire);
   }
-  float* scratch = g_scratch_addr[device];
+  const int sms = g_sm_count[device].load(std::memory_order_relaxed);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // Partial rows that fit in the scratch array; at least one block.
-  const long long max_blocks = kNoAllocScratchFloats / (static_cast<long long>(kWarps) * dim);
+  float* partial = scratch;
+  float* mid = scratch + kNoAllocPartialFloats;
+  // Partial rows that fit in their region; at least one block.
+  const long long max_blocks = kNoAllocPartialFloats / (static_cast<long long>(kWarps) * dim);
   if (max_blocks < 1) return ABACUS_NOALLOC_EBADSIZE;
-  const long long want = std::max<long long>(1, std::min<long long>((rows + kWarps - 1) / kWarps, 4LL * g_sm_count[device]));
+  const long long want = std::max<long long>(1, std::min<long long>((rows + kWarps - 1) / kWarps, 4LL * sms));
   const int nblocks = static_cast<int>(std::min(want, max_blocks));
   const int rows_per_block = rows == 0 ? 0 : (rows + nblocks - 1) / nblocks;
   const int vpl = (dim / 4 + 31) / 32;
   // Every partial row read below is written by this call (idle warps write
-  // zeros), so the scratch needs no clearing between calls.
+  // zeros), and every split sum is written before it is read, so the scratch
+  // needs no clearing between calls.
 #define ABACUS_NOALLOC_LAUNCH(V)                                                                                  \
-  rmsnorm_bwd_kernel<V><<<nblocks, kWarps * 32, 0, s>>>(dy, x, gamma, rstd, dx, scratch, rows, dim, rows_per_block)
+  rmsnorm_bwd_kernel<V><<<nblocks, kWarps * 32, 0, s>>>(dy, x, gamma, rstd, dx, partial, rows, dim, rows_per_block)
   if (vpl <= 2) ABACUS_NOALLOC_LAUNCH(2);
   else if (vpl <= 4) ABACUS_NOALLOC_LAUNCH(4);
   else if (vpl <= 8) ABACUS_NOALLOC_LAUNCH(8);
@@ -511,9 +530,19 @@ extern "C" __attribute__((visibility("default"))) int abacus_rmsnorm_bwd_noalloc
 #undef ABACUS_NOALLOC_LAUNCH
   err = cudaGetLastError();
   if (err != cudaSuccess) return static_cast<int>(err);
-  reduce_partials_kernel<<<(dim + 255) / 256, 256, 0, s>>>(scratch, dgamma, nblocks * kWarps, dim);
+  // Two-pass deterministic column sums of the partial rows (the regular
+  // backward's schedule), with the split sums in the second region.
+  const long long prow = static_cast<long long>(nblocks) * kWarps;
+  const long long max_splits = std::max<long long>(1, kNoAllocMidFloats / dim);
+  const long long splits = std::max<long long>(1, std::min<long long>({max_splits, 1024LL, (prow + 63) / 64}));
+  const long long per = (prow + splits - 1) / splits;
+  dim3 grid(static_cast<unsigned>((dim + 31) / 32), static_cast<unsigned>(splits));
+  colsum_split_kernel<<<grid, 256, 0, s>>>(partial, mid, prow, dim, per);
   err = cudaGetLastError();
   if (err != cudaSuccess) return static_cast<int>(err);
-  abacus::host::note_launch(2);
+  reduce_partials_kernel<<<(dim + 255) / 256, 256, 0, s>>>(mid, dgamma, static_cast<int>(splits), dim);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return static_cast<int>(err);
+  abacus::host::note_launch(3);
   return 0;
 }

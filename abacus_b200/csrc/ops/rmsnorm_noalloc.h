@@ -12,17 +12,21 @@
 //   dx[r, :]  = rstd[r] * gamma * dy[r, :]
 //               - x[r, :] * rstd[r]^3 * mean_j(gamma[j] * dy[r, j] * x[r, j])
 //   dgamma[:] = sum_r dy[r, :] * x[r, :] * rstd[r]
-// It gives the same results as the library's regular RMSNorm backward, which
-// allocates a temporary buffer for the dgamma reduction on every call. Here
-// that temporary lives in a fixed 4 MiB array in device memory that every GPU
-// loading this library holds until the process exits.
+// It runs the same kernels as the library's regular RMSNorm backward (a
+// row-parallel pass writing per-warp partial dgamma rows, then a two-pass
+// deterministic column sum), which allocates its reduction buffers on every
+// call. Here those buffers live in a fixed 4 MiB array in device memory that
+// every GPU loading this library holds until the process exits: 3 MiB of
+// partial rows and 1 MiB of per-split column sums.
 //
 // Arguments: device pointers to row-major fp32 data: dy, x, dx (rows x dim),
 // gamma, dgamma (dim), rstd (rows); `stream` is a cudaStream_t (may be null
 // for the legacy default stream). The call only enqueues work on `stream`.
 //
-// Limits: 0 < dim <= 4096 and dim % 4 == 0; pointers 16-byte aligned. Other
-// sizes are rejected with ABACUS_NOALLOC_EBADSIZE before anything is launched.
+// Limits: rows >= 0 (rows == 0 writes dgamma = 0 and leaves dx untouched),
+// 0 < dim <= 4096, dim % 4 == 0, and all six pointers non-null and 16-byte
+// aligned (the kernels move rows as float4). Anything else is rejected with
+// ABACUS_NOALLOC_EBADSIZE before anything is launched.
 //
 // Returns 0 on success, ABACUS_NOALLOC_EBADSIZE for rejected arguments, or a
 // cudaError_t value if a CUDA call fails.

@@ -2,27 +2,38 @@
 
 API and semantics follow ``abacus/distributed/data_parallel.py``: gradients
 are the token-weighted mean over every rank's targets (each rank's gradient is
-multiplied by its local count, summed, divided by the global count); stage 1
-shards the Adam moments, stage 2 also the gradients (reduce-scatter), stage 3
-also the parameters, gathered one unit (embedding, each block, final norm,
-root leftovers) at a time through module hooks. ``owned`` / ``grad_shards``
-feed the ZeRO-aware AdamW exactly as in the reference.
+multiplied by its local target count, summed over ranks, divided by the global
+count); stage 1 shards the Adam moments, stage 2 also the gradients, stage 3
+also the parameters. ``owned`` (``id(param) -> (begin, end)`` of the flattened
+parameter) and ``grad_shards`` feed the ZeRO-aware AdamW, and the sharding
+layout is the reference's: a unit's parameters laid end to end, cut into
+``world`` equal chunks with the tail of the last one padded.
 
-B200-first differences:
+Design (B200-first, NCCL collectives on the "dp" group of the installed mesh):
 
-* Stage 0 does not concatenate every gradient after backward. Gradients are
-  packed into ~25 MB buckets by post-accumulate hooks and each bucket's
-  all-reduce is launched asynchronously while backward continues. Buckets are
-  launched strictly in index order on every rank, so the NCCL call sequence is
-  identical across ranks even when a parameter receives no gradient.
-* The loss / token-count reduction is one 2-element all-reduce issued before
-  the buckets drain.
-* Collectives run on the "dp" group of the installed mesh (the world group
-  without one), so DP composes with TP / EP. Parameters listed in
-  ``exclude`` (e.g. expert weights sharded over the same ranks) are neither
-  broadcast nor reduced.
+* Stage 0: gradients are packed into ~25 MB buckets by post-accumulate hooks
+  and each bucket's all-reduce starts asynchronously while backward continues.
+  Buckets launch strictly in index order on every rank, so the NCCL call
+  sequence is identical across ranks even when a parameter gets no gradient.
+* Every ZeRO unit (:class:`_FlatUnit`) owns flat storage. Stages 1 / 2 keep
+  all parameters as views of one padded flat buffer, so the parameter
+  all-gather after the optimizer step is one in-place ``all_gather_into_tensor``
+  with no packing. Stage 3 keeps this rank's chunk of each unit as one
+  contiguous tensor whose pieces are the parameters' storage; a gather reads
+  the chunk directly.
+* Gradients of every stage are copied into the unit's flat gradient buffer as
+  they arrive (post-accumulate hooks) and the autograd gradient is released at
+  once. In stage 3 each unit's reduce-scatter starts asynchronously as soon as
+  its last gradient arrives, so it overlaps the rest of backward; the next
+  unit's parameter all-gather is prefetched one unit ahead in forward and in
+  backward.
+* The loss / token-count reduction is one 2-element all-reduce.
+* Parameters listed in ``exclude`` (e.g. expert weights sharded over the same
+  ranks) are neither broadcast nor reduced.
 """
 from __future__ import annotations
+
+import itertools
 
 import torch
 import torch.distributed as dist
@@ -36,37 +47,61 @@ def _has_parameters(module: torch.nn.Module) -> bool:
     return next(module.parameters(), None) is not None
 
 
-class _Partition:
-    """A flat parameter range, padded so every rank owns the same number of elements."""
+class _FlatUnit:
+    """One ZeRO unit: parameters in a flat index space cut into equal chunks.
 
-    def __init__(self, params: list[torch.nn.Parameter], rank: int, world_size: int):
+    Parameter i covers ``[starts[i], starts[i] + sizes[i])`` of a space of
+    ``total`` elements. The space is padded to ``padded = world * chunk`` and
+    rank r owns ``[r * chunk, (r + 1) * chunk)``. ``pieces[i] = (lo, hi, at)``:
+    elements ``[lo, hi)`` of parameter i's own flattened index lie in this
+    rank's chunk, starting at offset ``at`` of the chunk (``lo == hi``: none).
+    """
+
+    def __init__(self, params: list[torch.nn.Parameter], rank: int, world: int):
         if not params:
-            raise ValueError("parameter partition is empty")
-        self.params = params
-        self.shapes = [tuple(p.shape) for p in params]
-        self.numels = [p.numel() for p in params]
-        self.offsets = []
-        total = 0
-        for n in self.numels:
-            self.offsets.append(total)
-            total += n
-        self.total = total
-        self.shard = -(-total // world_size)
-        self.padded = self.shard * world_size
-        lo, hi = rank * self.shard, (rank + 1) * self.shard
-        self.owns: list[tuple[int, int]] = []
-        self.dests: list[int] = []
-        for off, n in zip(self.offsets, self.numels):
-            begin, stop = max(0, lo - off), min(n, hi - off)
-            if begin >= stop:
-                self.owns.append((0, 0))
-                self.dests.append(0)
-            else:
-                self.owns.append((begin, stop))
-                self.dests.append(max(off, lo) - lo)
-        self.shards: list[torch.Tensor] = []
-        self.gathered = False
-        self.pending: dict[int, torch.Tensor] = {}
+            raise ValueError("a ZeRO unit needs at least one parameter")
+        self.params = list(params)
+        self.shapes = [tuple(p.shape) for p in self.params]
+        self.sizes = [p.numel() for p in self.params]
+        self.starts = list(itertools.accumulate(self.sizes, initial=0))[:-1]
+        self.total = sum(self.sizes)
+        self.world = world
+        self.chunk = -(-self.total // world)
+        self.padded = self.chunk * world
+        first, last = rank * self.chunk, (rank + 1) * self.chunk
+        self.pieces: list[tuple[int, int, int]] = []
+        for start, size in zip(self.starts, self.sizes):
+            a, b = max(start, first), min(start + size, last)
+            self.pieces.append((a - start, b - start, a - first) if a < b else (0, 0, 0))
+        self.index = {id(p): i for i, p in enumerate(self.params)}
+        # Stage-3 parameter state.
+        self.local: torch.Tensor | None = None  # this rank's chunk of the values
+        self.full: torch.Tensor | None = None  # gathered values while materialised
+        self.gathering = None  # in-flight all-gather work
+        # Gradient state (every stage).
+        self.grad_flat: torch.Tensor | None = None
+        self.grad_chunk: torch.Tensor | None = None
+        self.arrived: set[int] = set()
+        self.scatter = None  # in-flight reduce-scatter work
+        self.reduced = False
+
+    def owned(self) -> dict[int, tuple[int, int]]:
+        return {id(p): (lo, hi) for p, (lo, hi, _) in zip(self.params, self.pieces) if lo < hi}
+
+    def piece_views(self, chunk: torch.Tensor) -> list[torch.Tensor]:
+        """This rank's piece of each parameter inside ``chunk`` (empty if none)."""
+        return [chunk[at : at + hi - lo] for lo, hi, at in self.pieces]
+
+    def param_views(self, flat: torch.Tensor) -> list[torch.Tensor]:
+        """Each parameter, shaped, inside a full flat buffer of the unit."""
+        return [flat[s : s + n].view(shape) for s, n, shape in zip(self.starts, self.sizes, self.shapes)]
+
+    def new_grad_flat(self) -> torch.Tensor:
+        p = self.params[0]
+        return torch.zeros(self.padded, dtype=p.dtype, device=p.device)
+
+    def reset(self) -> None:
+        self.arrived.clear()
         self.reduced = False
 
 
@@ -95,11 +130,12 @@ class DataParallel:
         exclude=None,
         dim: str = DIM,
         token_weighted: bool = True,
+        prefetch: bool = True,
     ):
         if not dist.is_initialized():
-            raise RuntimeError("Call init_process_group before DataParallel")
+            raise RuntimeError("DataParallel needs an initialised process group (call init_process_group first)")
         if stage not in (0, 1, 2, 3):
-            raise ValueError(f"zero stage must be 0, 1, 2, or 3, got {stage}")
+            raise ValueError(f"ZeRO stage {stage!r} is not one of 0, 1, 2, 3")
         self.model = model
         self.stage = stage
         self.dim = dim
@@ -114,7 +150,8 @@ class DataParallel:
         # gradients are plain sums (used when expert weights receive every
         # rank's tokens through the expert-parallel all-to-all).
         self.token_weighted = token_weighted
-        self.partitions: list[_Partition] = []
+        self.prefetch = prefetch
+        self.units: list[_FlatUnit] = []
         self.owned: dict[int, tuple[int, int]] | None = None
         self.grad_shards: dict[int, torch.Tensor] | None = None
         self._token_count = 0
@@ -122,6 +159,7 @@ class DataParallel:
         self._bucket_of: dict[int, tuple[int, int]] = {}
         self._next_launch = 0
         self._hooks_installed = False
+        self._flat_params: torch.Tensor | None = None  # stages 1 / 2
 
     # ------------------------------------------------------------------ helpers
     def _params(self):
@@ -130,13 +168,22 @@ class DataParallel:
     def _all_reduce(self, t, async_op=False):
         return dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group, async_op=async_op)
 
+    def _multiplier(self):
+        return self._token_count if self.token_weighted else 1.0
+
+    def _scale(self, t: torch.Tensor) -> None:
+        count = self._multiplier()
+        if isinstance(count, torch.Tensor):
+            t.mul_(count.to(t.dtype))
+        elif count != 1.0:
+            t.mul_(float(count))
+
     # ------------------------------------------------------------------ API
     def set_token_count(self, token_count) -> None:
         """This rank's target-token count for the coming backward (int or 0-d tensor)."""
         self._token_count = token_count
-        for part in self.partitions:
-            part.pending.clear()
-            part.reduced = False
+        for unit in self.units:
+            unit.reset()
         for b in self._buckets:
             b.ready.clear()
             b.work = None
@@ -152,16 +199,13 @@ class DataParallel:
         if self.stage == 0:
             self._install_buckets()
             return
-        self.partitions = []
         if self.stage == 3:
             self._install_stage3()
         else:
-            self.partitions.append(_Partition(self._params(), self.rank, self.world_size))
+            self._install_flat()
         self.owned = {}
-        for part in self.partitions:
-            for p, (b, e) in zip(part.params, part.owns):
-                if b != e:
-                    self.owned[id(p)] = (b, e)
+        for unit in self.units:
+            self.owned.update(unit.owned())
         self.grad_shards = {} if self.stage >= 2 else None
 
     @torch.no_grad()
@@ -170,33 +214,55 @@ class DataParallel:
         mean, total = self._mean_loss(loss, token_count)
         if self.stage == 0:
             self._finish_buckets(total)
-        elif self.stage == 1:
-            self._all_reduce_grads(token_count, total)
-        elif self.stage == 2:
-            self._reduce_scatter_grads(token_count, total)
         else:
-            self._scale_sharded_grads(total)
+            self._finish_units(total)
         return mean
 
     @torch.no_grad()
     def gather_parameters(self) -> None:
+        """Stages 1 / 2: every rank's updated chunk to every rank, in place."""
         if self.stage not in (1, 2):
             return
-        part = self.partitions[0]
-        flat = self._all_gather_unpadded(part, from_shards=False)
-        for p, off, n in zip(part.params, part.offsets, part.numels):
-            p.data.reshape(-1).copy_(flat[off : off + n])
+        unit = self.units[0]
+        mine = self._flat_params[self.rank * unit.chunk : (self.rank + 1) * unit.chunk]
+        dist.all_gather_into_tensor(self._flat_params, mine, group=self.group)
 
     @torch.no_grad()
     def full_parameters(self) -> list[torch.Tensor]:
         if self.stage < 3:
             return [p.detach().clone() for p in self.model.parameters()]
-        by_id = {}
-        for part in self.partitions:
-            flat = self._all_gather_unpadded(part, from_shards=True)
-            for p, off, n, shape in zip(part.params, part.offsets, part.numels, part.shapes):
-                by_id[id(p)] = flat[off : off + n].view(shape).clone()
-        return [by_id.get(id(p), p.detach().clone()) for p in self.model.parameters()]
+        full = {}
+        for unit in self.units:
+            flat = self._gather_chunks(unit.local)
+            for p, view in zip(unit.params, unit.param_views(flat)):
+                full[id(p)] = view.clone()
+        return [full.get(id(p), p.detach().clone()) for p in self.model.parameters()]
+
+    @torch.no_grad()
+    def gather_owned(self, pieces: dict[int, torch.Tensor]) -> dict[int, torch.Tensor]:
+        """Full flattened tensors from per-rank owned pieces (collective).
+
+        ``pieces`` maps ``id(param)`` to this rank's owned range of a per-element
+        quantity of that parameter (e.g. an Adam moment); the result maps every
+        parameter of the ZeRO units to its full flattened tensor.
+        """
+        out = {}
+        for unit in self.units:
+            p0 = unit.params[0]
+            chunk = torch.zeros(unit.chunk, dtype=p0.dtype, device=p0.device)
+            for p, view in zip(unit.params, unit.piece_views(chunk)):
+                src = pieces.get(id(p))
+                if src is not None and view.numel():
+                    view.copy_(src.reshape(-1))
+            flat = self._gather_chunks(chunk)
+            for p, s, n in zip(unit.params, unit.starts, unit.sizes):
+                out[id(p)] = flat[s : s + n].clone()
+        return out
+
+    def _gather_chunks(self, chunk: torch.Tensor) -> torch.Tensor:
+        flat = chunk.new_empty(chunk.numel() * self.world_size)
+        dist.all_gather_into_tensor(flat, chunk.contiguous(), group=self.group)
+        return flat
 
     # ------------------------------------------------------------------ loss
     def _mean_loss(self, loss, token_count):
@@ -209,7 +275,7 @@ class DataParallel:
         self._all_reduce(packed)
         total = packed[1]
         if not loss.is_cuda and total.item() == 0:
-            raise RuntimeError("no tokens contributed to the loss")
+            raise RuntimeError("no rank had a target token in this batch")
         return packed[0] / total, total
 
     # ------------------------------------------------------------------ stage 0
@@ -246,15 +312,8 @@ class DataParallel:
         bucket.ready.add(pi)
         self._launch_ready()
 
-    def _multiplier(self):
-        return self._token_count if self.token_weighted else 1.0
-
     def _launch(self, bucket):
-        count = self._multiplier()
-        if isinstance(count, torch.Tensor):
-            bucket.flat.mul_(count.to(bucket.flat.dtype))
-        else:
-            bucket.flat.mul_(float(count))
+        self._scale(bucket.flat)
         bucket.work = self._all_reduce(bucket.flat, async_op=True)
         bucket.launched = True
 
@@ -289,149 +348,158 @@ class DataParallel:
                 else:
                     p.grad.copy_(g)
 
-    # ------------------------------------------------------------------ stages 1-2
-    def _packed_grads(self, part, token_count):
-        flat = torch.zeros(part.padded, dtype=part.params[0].dtype, device=part.params[0].device)
-        for p, off, n in zip(part.params, part.offsets, part.numels):
-            if p.grad is None:
-                raise RuntimeError("backward produced no gradient for a parameter")
-            flat[off : off + n].copy_(p.grad.reshape(-1))
-        flat.mul_(torch.as_tensor(token_count if self.token_weighted else 1.0, dtype=flat.dtype, device=flat.device))
-        return flat
-
-    def _all_reduce_grads(self, token_count, total):
-        part = self.partitions[0]
-        flat = self._packed_grads(part, token_count)
-        self._all_reduce(flat)
-        flat = flat[: part.total] / total
-        for p, off, n in zip(part.params, part.offsets, part.numels):
-            p.grad.copy_(flat[off : off + n].view_as(p.grad))
-
-    def _reduce_scatter_grads(self, token_count, total):
-        part = self.partitions[0]
-        self._scatter_owned_grads(part, self._packed_grads(part, token_count), total)
-        for p in part.params:
-            p.grad = None
-
-    def _scale_sharded_grads(self, total):
-        for part in self.partitions:
-            if not part.reduced:
-                raise RuntimeError("backward produced no gradient for a parameter")
-            part.reduced = False
-        for g in self.grad_shards.values():
-            g.div_(total)
-
-    def _scatter_owned_grads(self, part, flat, total):
-        local = flat.new_empty(part.shard)
-        dist.reduce_scatter_tensor(local, flat, op=dist.ReduceOp.SUM, group=self.group)
-        if total is not None:
-            local.div_(total)
-        for p, (b, e), dest in zip(part.params, part.owns, part.dests):
-            if b != e:
-                self.grad_shards[id(p)] = local[dest : dest + (e - b)].clone()
+    # ------------------------------------------------------------------ stages 1 / 2
+    def _install_flat(self):
+        params = self._params()
+        unit = _FlatUnit(params, self.rank, self.world_size)
+        flat = torch.zeros(unit.padded, dtype=params[0].dtype, device=params[0].device)
+        for p, view in zip(params, unit.param_views(flat)):
+            view.copy_(p.data)
+            p.data = view
+        self._flat_params = flat
+        self.units = [unit]
+        self._hook_gradients(unit)
 
     # ------------------------------------------------------------------ stage 3
     def _install_stage3(self):
         covered = set()
+        modules = []
         for module in self._unit_modules():
-            params = [p for p in module.parameters() if id(p) not in self.excluded]
-            if not params:
-                continue
-            part = _Partition(params, self.rank, self.world_size)
-            self._materialize(part)
-            self.partitions.append(part)
-            covered.update(id(p) for p in params)
-            self._hook_module(module, part)
-        root = [p for p in self._params() if id(p) not in covered]
-        if root:
-            part = _Partition(root, self.rank, self.world_size)
-            self._materialize(part)
-            self.partitions.append(part)
-            self._hook_root(part)
+            params = [p for p in module.parameters() if id(p) not in self.excluded and id(p) not in covered]
+            if params:
+                modules.append((module, _FlatUnit(params, self.rank, self.world_size)))
+                covered.update(id(p) for p in params)
+        self.units = [unit for _, unit in modules]
+        rest = [p for p in self._params() if id(p) not in covered]
+        root = _FlatUnit(rest, self.rank, self.world_size) if rest else None
+        if root is not None:
+            self.units.append(root)
+        for unit in self.units:
+            self._shard(unit)
+            self._hook_gradients(unit)
+        # Forward order of the module units; the root unit (the LM head and
+        # any other leftover) is used after the last one.
+        order = [unit for _, unit in modules]
+        for k, (module, unit) in enumerate(modules):
+            after = order[k + 1] if k + 1 < len(order) else root
+            before = order[k - 1] if k > 0 else None
+            module.register_forward_pre_hook(lambda _m, _a, u=unit, nxt=after: self._enter(u, nxt))
+            module.register_forward_hook(lambda _m, _a, _o, u=unit: self._leave(u))
+            module.register_full_backward_pre_hook(lambda _m, _g, u=unit, nxt=before: self._enter(u, nxt))
+        if root is not None:
+            last = modules[-1][0] if modules else None
+            if last is not None:
+                last.register_forward_hook(lambda _m, _a, _o, u=root: self._materialize(u))
+            else:
+                self.model.register_forward_pre_hook(lambda _m, _a, u=root: self._materialize(u))
+            self.model.register_forward_hook(lambda _m, _a, _o, u=root: self._leave(u))
+            tail = order[-1] if order else None
+            self.model.register_full_backward_pre_hook(lambda _m, _g, u=root, nxt=tail: self._enter(u, nxt))
 
     def _unit_modules(self):
+        """Embedding, each block, the final norm (in forward order); a model
+        without a ``blocks`` list is one unit."""
         blocks = getattr(self.model, "blocks", None)
         if not isinstance(blocks, torch.nn.ModuleList):
             return [self.model]
-        modules = []
-        emb = getattr(self.model, "embedding", None)
-        if emb is not None and _has_parameters(emb):
-            modules.append(emb)
-        modules.extend(b for b in blocks if _has_parameters(b))
-        norm = getattr(self.model, "norm", None)
-        if norm is not None and _has_parameters(norm):
-            modules.append(norm)
-        return modules
-
-    def _materialize(self, part):
-        for p, (b, e) in zip(part.params, part.owns):
-            shard = p.data.new_empty(0) if b == e else p.data.reshape(-1)[b:e].detach().clone()
-            part.shards.append(shard)
-        for p, shard in zip(part.params, part.shards):
-            p.data = shard
-        part.gathered = False
-
-    def _hook_module(self, module, part):
-        module.register_forward_pre_hook(lambda _m, _a, part=part: self._gather(part))
-        module.register_forward_hook(lambda _m, _a, _o, part=part: self._reshard(part))
-        module.register_full_backward_pre_hook(lambda _m, _g, part=part: self._gather(part))
-        for p in part.params:
-            p.register_post_accumulate_grad_hook(lambda q, part=part: self._on_grad_stage3(q, part))
-
-    def _hook_root(self, part):
-        norm = getattr(self.model, "norm", None)
-        if isinstance(norm, torch.nn.Module):
-            norm.register_forward_hook(lambda _m, _a, _o, part=part: self._gather(part))
-        else:
-            self.model.register_forward_pre_hook(lambda _m, _a, part=part: self._gather(part))
-        self.model.register_forward_hook(lambda _m, _a, _o, part=part: self._reshard(part))
-        self.model.register_full_backward_pre_hook(lambda _m, _g, part=part: self._gather(part))
-        for p in part.params:
-            p.register_post_accumulate_grad_hook(lambda q, part=part: self._on_grad_stage3(q, part))
+        found = [getattr(self.model, "embedding", None), *blocks, getattr(self.model, "norm", None)]
+        return [m for m in found if isinstance(m, torch.nn.Module) and _has_parameters(m)]
 
     @torch.no_grad()
-    def _gather(self, part):
-        if part.gathered:
+    def _shard(self, unit: _FlatUnit) -> None:
+        p0 = unit.params[0]
+        unit.local = torch.zeros(unit.chunk, dtype=p0.dtype, device=p0.device)
+        for p, (lo, hi, _), view in zip(unit.params, unit.pieces, unit.piece_views(unit.local)):
+            if lo < hi:
+                view.copy_(p.data.reshape(-1)[lo:hi])
+        self._to_local(unit)
+
+    def _to_local(self, unit: _FlatUnit) -> None:
+        for p, view in zip(unit.params, unit.piece_views(unit.local)):
+            p.data = view
+        unit.full = None
+
+    def _start_gather(self, unit: _FlatUnit | None) -> None:
+        if unit is None or unit.full is not None or unit.gathering is not None:
             return
-        flat = self._all_gather_unpadded(part, from_shards=True)
-        for p, off, n, shape in zip(part.params, part.offsets, part.numels, part.shapes):
-            p.data = flat[off : off + n].view(shape)
-        part.gathered = True
+        flat = unit.local.new_empty(unit.padded)
+        work = dist.all_gather_into_tensor(flat, unit.local, group=self.group, async_op=True)
+        unit.gathering = (flat, work)
 
     @torch.no_grad()
-    def _reshard(self, part):
-        if not part.gathered:
+    def _materialize(self, unit: _FlatUnit) -> None:
+        if unit.full is not None:
             return
-        for p, shard in zip(part.params, part.shards):
-            p.data = shard
-        part.gathered = False
+        self._start_gather(unit)
+        flat, work = unit.gathering
+        work.wait()
+        unit.gathering = None
+        unit.full = flat
+        for p, view in zip(unit.params, unit.param_views(flat)):
+            p.data = view
 
     @torch.no_grad()
-    def _on_grad_stage3(self, p, part):
-        if p.grad is None:
-            raise RuntimeError("backward produced no gradient for a parameter")
-        if id(p) in part.pending:
-            raise RuntimeError("gradient accumulated twice for one parameter")
-        part.pending[id(p)] = p.grad.detach()
+    def _enter(self, unit: _FlatUnit, upcoming: _FlatUnit | None) -> None:
+        self._materialize(unit)
+        if self.prefetch:
+            self._start_gather(upcoming)
+
+    @torch.no_grad()
+    def _leave(self, unit: _FlatUnit) -> None:
+        # The autograd graph holds the parameter objects, not these values;
+        # backward's pre-hook materialises them again before they are read.
+        if unit.full is not None:
+            self._to_local(unit)
+
+    # ------------------------------------------------------------------ gradients (stages 1-3)
+    def _hook_gradients(self, unit: _FlatUnit) -> None:
+        for p in unit.params:
+            p.register_post_accumulate_grad_hook(lambda q, u=unit: self._grad_arrived(u, q))
+
+    @torch.no_grad()
+    def _grad_arrived(self, unit: _FlatUnit, p) -> None:
+        i = unit.index[id(p)]
+        if i in unit.arrived:
+            raise RuntimeError(f"a {tuple(p.shape)} parameter received a second gradient in one backward")
+        if unit.grad_flat is None:
+            unit.grad_flat = unit.new_grad_flat()
+        s, n = unit.starts[i], unit.sizes[i]
+        unit.grad_flat[s : s + n].copy_(p.grad.reshape(-1))
         p.grad = None
-        if len(part.pending) != len(part.params):
-            return
-        flat = torch.zeros(part.padded, dtype=p.dtype, device=p.device)
-        for q, off, n in zip(part.params, part.offsets, part.numels):
-            flat[off : off + n].copy_(part.pending[id(q)].reshape(-1))
-        flat.mul_(torch.as_tensor(self._multiplier(), dtype=flat.dtype, device=flat.device))
-        self._scatter_owned_grads(part, flat, None)
-        part.pending.clear()
-        self._reshard(part)
-        part.reduced = True
+        unit.arrived.add(i)
+        if len(unit.arrived) == len(unit.params):
+            self._start_reduce(unit)
+            if self.stage == 3:
+                self._leave(unit)
 
-    def _all_gather_unpadded(self, part, from_shards):
-        local = torch.zeros(part.shard, dtype=part.params[0].dtype, device=part.params[0].device)
-        for i, (p, (b, e), dest) in enumerate(zip(part.params, part.owns, part.dests)):
-            if b == e:
-                continue
-            src = part.shards[i] if from_shards else p.data.reshape(-1)[b:e]
-            local[dest : dest + (e - b)].copy_(src)
-        gathered = local.new_empty(part.padded)
-        dist.all_gather_into_tensor(gathered, local, group=self.group)
-        return gathered[: part.total]
+    def _start_reduce(self, unit: _FlatUnit) -> None:
+        self._scale(unit.grad_flat)
+        if self.stage == 1:
+            unit.scatter = self._all_reduce(unit.grad_flat, async_op=True)
+            return
+        if unit.grad_chunk is None:
+            unit.grad_chunk = unit.grad_flat.new_empty(unit.chunk)
+        unit.scatter = dist.reduce_scatter_tensor(unit.grad_chunk, unit.grad_flat, op=dist.ReduceOp.SUM,
+                                                  group=self.group, async_op=True)
+
+    def _finish_units(self, total) -> None:
+        for unit in self.units:
+            if len(unit.arrived) != len(unit.params):
+                raise RuntimeError("backward produced no gradient for some parameter of a ZeRO unit")
+            if unit.scatter is None:
+                self._start_reduce(unit)
+        for unit in self.units:
+            unit.scatter.wait()
+            unit.scatter = None
+            unit.reduced = True
+            if self.stage == 1:
+                unit.grad_flat.div_(total)
+                for p, view in zip(unit.params, unit.param_views(unit.grad_flat)):
+                    p.grad = view
+            else:
+                unit.grad_chunk.div_(total)
+                for p, view in zip(unit.params, unit.piece_views(unit.grad_chunk)):
+                    if view.numel():
+                        self.grad_shards[id(p)] = view
+            # The next backward fills a fresh buffer (in stage 1 p.grad keeps this one).
+            unit.grad_flat = None

@@ -2,9 +2,12 @@
 
 Semantics follow ``abacus/distributed/expert_parallel.py``:
 
-* ``shard_counts`` (``:16-19``): contiguous token shards, remainder first.
-* ``exchange_counts`` (``:22-26``): all-to-all of per-rank counts.
-* ``_AllToAll`` (``:29-59``): variable-size exchange; backward swaps splits.
+* ``shard_counts`` (``:16-19``): contiguous token shards, remainder first
+  (closed form here).
+* ``exchange_counts`` (``:22-26``): receive counts from send counts (here the
+  column of an all-gathered send-count matrix).
+* ``_AllToAll`` (``:29-59``): variable-size exchange whose adjoint is the
+  swapped exchange.
 * ``_GatherTokenShards`` (``:62-86``): all-gather-v of the shard outputs;
   backward keeps this rank's slice.
 * ``_SumReplicatedGrads`` (``:89-102``): identity forward, all-reduce backward.
@@ -29,47 +32,53 @@ def _rank_and_world_size(dim: str = DIM) -> tuple[int, int]:
 
 
 def shard_counts(tokens: int, world_size: int) -> list[int]:
-    """Contiguous token shards"""
-    base, extra = divmod(tokens, world_size)
-    return [base + (1 if rank < extra else 0) for rank in range(world_size)]
+    """Split ``tokens`` rows into ``world_size`` contiguous runs; the first
+    ``tokens % world_size`` runs are one row longer."""
+    return [(tokens + world_size - 1 - r) // world_size for r in range(world_size)]
 
 
 def exchange_counts(input_splits: torch.Tensor, dim: str = DIM) -> torch.Tensor:
-    """One count per rank. output[i] is how many rows rank i sends here."""
-    output_splits = torch.empty_like(input_splits)
-    dist.all_to_all_single(output_splits, input_splits.contiguous(), group=_mesh.group_for(dim))
-    return output_splits
+    """Receive counts from send counts: entry i of the result is the number of
+    rows rank i sends to this rank.
+
+    Every rank contributes its send-count vector to a (P, P) matrix whose row
+    r is rank r's sends; this rank's receive counts are the matrix's column.
+    """
+    rank, world = _rank_and_world_size(dim)
+    sends = input_splits.reshape(-1).contiguous()
+    if world == 1:
+        return sends.clone()
+    matrix = sends.new_empty(world * sends.numel())
+    dist.all_gather_into_tensor(matrix, sends, group=_mesh.group_for(dim))
+    return matrix.view(world, -1)[:, rank].contiguous()
+
+
+def _as_sizes(counts) -> list[int]:
+    return [int(c) for c in (counts.tolist() if torch.is_tensor(counts) else counts)]
+
+
+def _exchange_rows(rows: torch.Tensor, send: list[int], recv: list[int], dim: str) -> torch.Tensor:
+    out = rows.new_empty((sum(recv), *rows.shape[1:]))
+    dist.all_to_all_single(out, rows.contiguous(), output_split_sizes=recv, input_split_sizes=send,
+                           group=_mesh.group_for(dim))
+    return out
 
 
 class _AllToAll(torch.autograd.Function):
-    """Variable-size token exchange. Backward swaps the split directions."""
+    """Row exchange with per-peer sizes (``send[i]`` rows go to rank i,
+    ``recv[i]`` arrive from it). The exchange is linear and its adjoint is the
+    same exchange with the size lists swapped, which is the backward."""
 
     @staticmethod
     def forward(ctx, tokens, input_splits, output_splits, dim: str = DIM):
-        ctx.input_splits = [int(s) for s in input_splits.tolist()]
-        ctx.output_splits = [int(s) for s in output_splits.tolist()]
-        ctx.dim = dim
-        out = tokens.new_empty(sum(ctx.output_splits), *tokens.shape[1:])
-        dist.all_to_all_single(
-            out,
-            tokens.detach().contiguous(),
-            output_split_sizes=ctx.output_splits,
-            input_split_sizes=ctx.input_splits,
-            group=_mesh.group_for(dim),
-        )
-        return out
+        send, recv = _as_sizes(input_splits), _as_sizes(output_splits)
+        ctx.adjoint = (recv, send, dim)
+        return _exchange_rows(tokens.detach(), send, recv, dim)
 
     @staticmethod
     def backward(ctx, grad):
-        out = grad.new_empty(sum(ctx.input_splits), *grad.shape[1:])
-        dist.all_to_all_single(
-            out,
-            grad.detach().contiguous(),
-            output_split_sizes=ctx.input_splits,
-            input_split_sizes=ctx.output_splits,
-            group=_mesh.group_for(ctx.dim),
-        )
-        return out, None, None, None
+        send, recv, dim = ctx.adjoint
+        return _exchange_rows(grad.detach(), send, recv, dim), None, None, None
 
 
 class _GatherTokenShards(torch.autograd.Function):

@@ -7,8 +7,8 @@ cudaFree. For them the library exports one C function that runs the RMSNorm
 backward with its reduction scratch in a fixed device array instead of a
 per-call buffer. This test calls that function through its exported C symbol
 (ctypes, raw device pointers, the current stream) and checks it against the
-library's regular backward on two calls in a row, since every call reuses the
-same scratch array.
+library's regular backward and against a plain fp32 PyTorch autograd RMSNorm,
+on two calls in a row, since every call reuses the same scratch array.
 """
 import ctypes
 
@@ -45,6 +45,15 @@ def _case(rows, dim, seed):
     return dy, x, gamma, rstd
 
 
+def _autograd_oracle(dy, x, gamma, eps=1e-5):
+    """dx, dgamma of y = gamma * x * rsqrt(mean(x^2) + eps) by fp32 autograd."""
+    xr = x.detach().clone().requires_grad_(True)
+    gr = gamma.detach().clone().requires_grad_(True)
+    y = gr * xr * torch.rsqrt(xr.square().mean(-1, keepdim=True) + eps)
+    y.backward(dy)
+    return xr.grad, gr.grad
+
+
 def _close(a, b, tol=1e-5):
     err = ((a.double() - b.double()).abs().max() / b.double().abs().max()).item()
     assert err < tol, f"rel err {err:.3e}"
@@ -66,6 +75,28 @@ def test_no_alloc_entry_point_matches_regular_backward(rows, dim):
         check_status()
         _close(dx, dx_ref)
         _close(dg, dg_ref)
+        dx_ag, dg_ag = _autograd_oracle(dy, x, gamma)
+        _close(dx, dx_ag, tol=1e-4)
+        _close(dg, dg_ag, tol=1e-4)
+
+
+def test_no_alloc_entry_point_zero_rows():
+    fn = _entry_point()
+    dim = 768
+    # Real buffers (an empty tensor has no address), passed with rows = 0.
+    x = torch.zeros(1, dim, device="cuda")
+    dx = torch.full((1, dim), 7.0, device="cuda")
+    rstd = torch.ones(4, device="cuda")
+    gamma = torch.ones(dim, device="cuda")
+    dg = torch.full((dim,), float("nan"), device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for _ in range(2):
+        ptrs = [t.data_ptr() for t in (x, x, gamma, rstd, dx, dg)]
+        assert fn(*ptrs, 0, dim, stream) == 0
+        torch.cuda.synchronize()
+        check_status()
+        assert torch.equal(dg, torch.zeros_like(dg))
+        assert torch.equal(dx, torch.full_like(dx, 7.0))  # dx untouched
 
 
 def test_no_alloc_entry_point_rejects_unsupported_sizes():
@@ -75,3 +106,21 @@ def test_no_alloc_entry_point_rejects_unsupported_sizes():
         vec = torch.zeros(dim, device="cuda")
         rstd = torch.ones(2, device="cuda")
         assert _call(fn, x, x, vec, rstd, x, vec) == EBADSIZE
+
+
+def test_no_alloc_entry_point_rejects_misaligned_pointers():
+    """A row view starting 4 bytes into a buffer is refused before launch."""
+    fn = _entry_point()
+    rows, dim = 8, 64
+    buf = torch.zeros(rows * dim + 4, device="cuda")
+    x = buf[1:1 + rows * dim].view(rows, dim)  # 4-byte offset
+    good = torch.zeros(rows, dim, device="cuda")
+    vec = torch.ones(dim, device="cuda")
+    rstd = torch.ones(rows, device="cuda")
+    assert x.data_ptr() % 16 == 4
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for args in ((x, good, vec, rstd, good, vec), (good, good, vec, rstd, x, vec)):
+        ptrs = [a.data_ptr() for a in args]
+        assert fn(*ptrs, rows, dim, stream) == EBADSIZE
+    torch.cuda.synchronize()
+    check_status()

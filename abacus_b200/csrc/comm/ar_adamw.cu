@@ -190,7 +190,7 @@ void symm_barrier(std::vector<int64_t> signal_ptrs, int64_t rank, int64_t slot_b
 
 void ar_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, torch::Tensor counts,
               bool normalize, int64_t rank, int64_t lo, int64_t hi, torch::Tensor exp_avg, torch::Tensor exp_avg_sq,
-              double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step) {
+              double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step, int64_t max_ctas) {
   const c10::cuda::CUDAGuard guard(exp_avg.device());
   TORCH_CHECK(lo % 4 == 0 && hi % 4 == 0 && hi >= lo, "owned range must be float4 aligned");
   TORCH_CHECK(exp_avg.is_contiguous() && exp_avg_sq.is_contiguous() && exp_avg.numel() == hi - lo &&
@@ -209,7 +209,10 @@ void ar_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, t
   const float bc2s = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
   const long long n4 = (hi - lo) / 4;
   const int sms = at::cuda::getDeviceProperties(exp_avg.device().index())->multiProcessorCount;
-  const int grid = static_cast<int>(std::min<long long>((n4 + 255) / 256, 8LL * sms));
+  // max_ctas > 0 caps the grid, so a reduction that runs beside other
+  // kernels (under backward) leaves them most of the SMs.
+  const long long cap = max_ctas > 0 ? max_ctas : 8LL * sms;
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((n4 + 255) / 256, cap)));
   ar_adamw_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       t, static_cast<int>(rank), static_cast<int>(grad_ptrs.size()), lo / 4, hi / 4, exp_avg.data_ptr<float>(),
       exp_avg_sq.data_ptr<float>(), static_cast<float>(lr), static_cast<float>(beta1), static_cast<float>(beta2),

@@ -1,6 +1,8 @@
 """Training loop (``abacus/trainer.py``): forward -> cross entropy ->
 zero_grad -> backward -> data-parallel sync -> WSD learning rate -> AdamW ->
-ZeRO parameter gather; plus the pipeline and context-parallel branches.
+ZeRO parameter gather; plus the pipeline and context-parallel branches. With
+the fused data-parallel optimizer the learning rate is taken before backward
+and the reduction + AdamW run per gradient bucket under backward.
 
 Differences from the reference, none of which change the maths:
 
@@ -81,6 +83,8 @@ class Trainer:
             owned=owned, grad_shards=grad_shards,
         )
         self._fused = bool(getattr(parallel, "fused_optimizer", False))
+        if self._fused and pipeline is not None:
+            raise ValueError("the fused data-parallel optimizer does not combine with pipeline parallel")
         if self._fused:
             parallel.bind_optimizer(self.optimizer)
         self.scheduler = WSD(total_steps, lr=schedule_lr) if total_steps is not None else None
@@ -120,11 +124,18 @@ class Trainer:
             print_peak_memory()
         if self.parallel is not None:
             self.parallel.set_token_count(token_count)
+        if self._fused:
+            # The fused data-parallel path reduces and updates each gradient
+            # bucket while backward runs, so this step's learning rate and
+            # token count are fixed before backward.
+            self._advance_lr()
+            self.parallel.prepare_step(self.optimizer, token_count)
         loss.backward()
         local_loss = loss.detach()
         if self.parallel is not None:
             loss = self.parallel.synchronize(loss, token_count)
-        self._optimizer_step()
+        if not self._fused:
+            self._optimizer_step()
         if self.parallel is not None:
             self.parallel.gather_parameters()
         return loss.detach(), local_loss
@@ -137,14 +148,13 @@ class Trainer:
                 loss = loss + extra
         return loss
 
-    def _optimizer_step(self) -> None:
+    def _advance_lr(self) -> None:
         if self.scheduler is not None:
             self.optimizer.lr = self.scheduler.step()
-        if self._fused:
-            # Gradient reduction, AdamW and the parameter broadcast in one kernel.
-            self.parallel.step_optimizer(self.optimizer)
-        else:
-            self.optimizer.step()
+
+    def _optimizer_step(self) -> None:
+        self._advance_lr()
+        self.optimizer.step()
 
     def _context_parallel_active(self) -> bool:
         if not getattr(self.model, "context_parallel", False):

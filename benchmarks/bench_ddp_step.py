@@ -65,7 +65,7 @@ def main():
     # part of backward in both paths).
     fused_model = Transformer(dim=768, n_heads=12, head_dim=64, n_blocks=12, vocab_size=50304,
                               hidden_dim=2048).cuda()
-    dp = FusedDataParallel(fused_model)
+    dp = FusedDataParallel(fused_model, overlap=False)
     dp.broadcast_parameters()
     fopt = AdamW(fused_model, owned=dp.owned)
     dp.bind_optimizer(fopt)
@@ -74,10 +74,10 @@ def main():
     count = torch.tensor(1000, device="cuda")
 
     def fused():
-        dp.set_token_count(count)
-        dp._ready.update(range(len(dp._flat_params)))
+        dp.prepare_step(fopt, count)
+        for b in dp.flat_buckets:
+            b.arrived.update(b.members)
         dp.synchronize(loss, count)
-        dp.step_optimizer(fopt)
 
     t_fused = timed(fused)
     dp.check()

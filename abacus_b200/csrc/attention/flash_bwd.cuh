@@ -141,6 +141,11 @@ struct DkdvCfg {
   static constexpr int kStageBytes = 4 * kQTile * kSplit;  // Q_k, Q_mn, dO_k, dO_mn [+ lo]
   static constexpr int kSmemBytes = 2 * kKVTile * kSplit + kStageBytes + 1024;
   static constexpr int kThreads = PASSES == 3 ? 320 : 192;
+  // Register cap for one CTA per SM: each of the 4 SM sub-partitions holds
+  // 16384 registers and ceil(warps / 4) of the CTA's warps.
+  static constexpr int kWarpsPerSubpartition = (kThreads / 32 + 3) / 4;
+  static constexpr int kMaxRegs =
+      (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8 > 255 ? 255 : (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8;
   // TMEM: ST (S^T, P^T hi [, P^T lo]), DPT (dP^T, dS^T hi [, dS^T lo]),
   // dV, dK partials [+ dV, dK masters in 3xTF32 mode].
   static constexpr int kSTCols = kInner * kSplit;
@@ -152,7 +157,7 @@ struct DkdvCfg {
 };
 
 template <int D, int PASSES>
-__global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkdv_kernel(const __grid_constant__ BwdParams p) {
+__global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kernel(const __grid_constant__ BwdParams p) {
   using Cfg = DkdvCfg<D, PASSES>;
   constexpr int NQ = Cfg::kInner;
   static_assert(Cfg::kCols <= 512, "TMEM budget");
@@ -385,14 +390,14 @@ __global__ void __launch_bounds__(DkdvCfg<D, PASSES>::kThreads, 1) flash_bwd_dkd
           const bool valid = !partial || (ki < p.lk && qpos_t >= kpos);
           const float lse2 = __shfl_sync(0xffffffffu, lse_l[c], t);
           const float dl_ = __shfl_sync(0xffffffffu, dl_l[c], t);
-          const float pr = valid ? exp2f(__uint_as_float(sv32[t]) * p.scale_log2 - lse2) : 0.f;
+          const float pr = valid ? ex2_approx(__uint_as_float(sv32[t]) * p.scale_log2 - lse2) : 0.f;
           const float ds = pr * (__uint_as_float(dp32[t]) - dl_);
           if (PASSES == 3) {
-            const float a = to_tf32(pr), d2 = to_tf32(ds);
+            const float a = to_tf32_alu(pr), d2 = to_tf32_alu(ds);
             sv32[t] = __float_as_uint(a);
-            pl[t] = __float_as_uint(to_tf32(pr - a));
+            pl[t] = __float_as_uint(to_tf32_alu(pr - a));
             dp32[t] = __float_as_uint(d2);
-            dl[t] = __float_as_uint(to_tf32(ds - d2));
+            dl[t] = __float_as_uint(to_tf32_alu(ds - d2));
           } else {
             sv32[t] = __float_as_uint(pr);
             dp32[t] = __float_as_uint(ds);
@@ -517,6 +522,11 @@ struct DqCfg {
   static constexpr int kStageBytes = 3 * kKTile * kSplit;  // K_k, K_mn, V_k [+ lo]
   static constexpr int kSmemBytes = 2 * kQTile * kSplit + kStageBytes + 1024;
   static constexpr int kThreads = PASSES == 3 ? 320 : 192;
+  // Register cap for one CTA per SM: each of the 4 SM sub-partitions holds
+  // 16384 registers and ceil(warps / 4) of the CTA's warps.
+  static constexpr int kWarpsPerSubpartition = (kThreads / 32 + 3) / 4;
+  static constexpr int kMaxRegs =
+      (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8 > 255 ? 255 : (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8;
   // TMEM: S, dP (dS hi [, dS lo]), dQ partials x2.
   static constexpr int kS = 0, kDP = kInner, kDQ = kInner + kInner * kSplit;
   static constexpr int kCols = kDQ + 2 * D;
@@ -525,7 +535,7 @@ struct DqCfg {
 };
 
 template <int D, int PASSES>
-__global__ void __launch_bounds__(DqCfg<D, PASSES>::kThreads, 1) flash_bwd_dq_kernel(const __grid_constant__ BwdParams p) {
+__global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(const __grid_constant__ BwdParams p) {
   using Cfg = DqCfg<D, PASSES>;
   constexpr int NK = Cfg::kInner;
   static_assert(Cfg::kCols <= 512, "TMEM budget");
@@ -733,12 +743,12 @@ __global__ void __launch_bounds__(DqCfg<D, PASSES>::kThreads, 1) flash_bwd_dq_ke
           const int ki = kbk * NK + c * 32 + t;
           bool valid = true;
           if (partial) valid = qi < p.lq && ki < p.lk && (p.k_pos ? static_cast<int>(__ldg(p.k_pos + ki)) : ki) <= qpos;
-          const float pr = valid ? exp2f(__uint_as_float(sv32[t]) * p.scale_log2 - lse2) : 0.f;
+          const float pr = valid ? ex2_approx(__uint_as_float(sv32[t]) * p.scale_log2 - lse2) : 0.f;
           const float ds = pr * (__uint_as_float(dp32[t]) - dl_);
           if (PASSES == 3) {
-            const float a = to_tf32(ds);
+            const float a = to_tf32_alu(ds);
             dp32[t] = __float_as_uint(a);
-            sv32[t] = __float_as_uint(to_tf32(ds - a));
+            sv32[t] = __float_as_uint(to_tf32_alu(ds - a));
           } else {
             dp32[t] = __float_as_uint(ds);
           }

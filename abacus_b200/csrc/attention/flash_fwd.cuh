@@ -4,7 +4,9 @@
 // 64; blocks entirely in the masked future are skipped (positions may be the
 // global zigzag positions of context parallelism).
 //
-//   warp 0      TMA producer: Q once, then K_j / V_j into a 2-stage ring
+//   warp 0      TMA producer: Q once, then K_j and V_j into two 2-slot rings
+//               with their own barriers: a K slot is free as soon as S_j has
+//               read it, a V slot once PV_j has, so K runs one block ahead
 //   warp 1      TMEM allocator + single-thread MMA issuer
 //                 S_j  = Q K_j^T          (A, B from smem, K-major)
 //                 PV_j = P_j V_j          (A = P from TMEM, B = V MN-major)
@@ -67,6 +69,11 @@ struct FwdCfg {
   static constexpr int kStageBytes = (kKBytes + kVBytes) * kSplit;
   static constexpr int kSmemBytes = kQBytes * kSplit + kStages * kStageBytes + 1024;
   static constexpr int kThreads = PASSES == 3 ? 320 : 192;
+  // Register cap for one CTA per SM: each of the 4 SM sub-partitions holds
+  // 16384 registers and ceil(warps / 4) of the CTA's warps.
+  static constexpr int kWarpsPerSubpartition = (kThreads / 32 + 3) / 4;
+  static constexpr int kMaxRegs =
+      (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8 > 255 ? 255 : (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8;
   static constexpr int kSPCols = kBlockN * (PASSES == 3 ? 2 : 1);  // S / P hi [/ P lo]
   static constexpr int kPVBase = 2 * kSPCols;
   static constexpr int kCols = kPVBase + 2 * D;
@@ -74,16 +81,15 @@ struct FwdCfg {
   static constexpr int kMaxBlocks = 2048;  // key blocks per sequence (Lk <= 131072)
 };
 
-__device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }
 
 template <int D, int PASSES>
-__global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kernel(const __grid_constant__ FwdParams p) {
+__global__ void __maxnreg__((FwdCfg<D, PASSES>::kMaxRegs)) flash_fwd_kernel(const __grid_constant__ FwdParams p) {
   using Cfg = FwdCfg<D, PASSES>;
   static_assert(D % 32 == 0 && D <= 128, "head_dim must be 32, 64, 96 or 128");
   static_assert(Cfg::kCols <= 512, "TMEM budget");
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t q_full, q_conv;
-  __shared__ uint64_t kv_full[2], kv_conv[2], kv_empty[2];
+  __shared__ uint64_t k_full[2], k_conv[2], k_empty[2], v_full[2], v_conv[2], v_empty[2];
   __shared__ uint64_t s_full[2], p_full[2], pv_full[2], pv_empty[2];
   __shared__ uint32_t tmem_slot;
   __shared__ int n_blocks;
@@ -91,6 +97,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const bool traced = p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+
 #define ABACUS_FWD_TRACE(slot, j) \
   if (traced && (j) < 64) p.trace[(slot) * 64 + (j)] = clock64();
   if (threadIdx.x == 0) ABACUS_FWD_TRACE(8, 0)
@@ -132,9 +139,12 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
     mbar_init(&q_full, 1);
     mbar_init(&q_conv, 128);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_conv[i], 128);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_conv[i], 128);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_conv[i], 128);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&pv_full[i], 1);
@@ -208,23 +218,40 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
       mbar_arrive_expect_tx(&q_full, Cfg::kQBytes);
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) tma_load_2d(sq + c * kBlockM * 128, &p.tma_q, &q_full, col0 + 32 * c, q_row0);
-      int issued = 0;
-      for (int j = 0; j < nb; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
-        const int kb = block_list[j] & 0xFFFF;
-        const int krow = k_row0 + kb * kBlockN;
-        ABACUS_FWD_TRACE(0, j)
-        mbar_arrive_expect_tx(&kv_full[s], Cfg::kKBytes + Cfg::kVBytes);
+      // K runs one block ahead of V: K_j is needed by S_j, V_j only by PV_j,
+      // which follows the softmax of block j.
+      int issued_k = 0, issued_v = 0;
+      bool ok = true;
+      for (int j = 0; j <= nb && ok; ++j) {
+        if (j < nb) {
+          const int s = j & 1;
+          if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+          ABACUS_FWD_TRACE(0, j)
+          const int krow = k_row0 + (block_list[j] & 0xFFFF) * kBlockN;
+          mbar_arrive_expect_tx(&k_full[s], Cfg::kKBytes);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          tma_load_2d(k_hi(s) + c * kBlockN * 128, &p.tma_k, &kv_full[s], col0 + 32 * c, krow);
-          tma_load_2d(v_hi(s) + c * kBlockN * 128, &p.tma_v, &kv_full[s], col0 + 32 * c, krow);
+          for (int c = 0; c < D / 32; ++c)
+            tma_load_2d(k_hi(s) + c * kBlockN * 128, &p.tma_k, &k_full[s], col0 + 32 * c, krow);
+          ++issued_k;
         }
-        ++issued;
+        if (j >= 1) {
+          const int jv = j - 1, s = jv & 1;
+          if (jv >= 2 && !mbar_wait(&v_empty[s], ((jv >> 1) - 1) & 1, p.status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          const int vrow = k_row0 + (block_list[jv] & 0xFFFF) * kBlockN;
+          mbar_arrive_expect_tx(&v_full[s], Cfg::kVBytes);
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c)
+            tma_load_2d(v_hi(s) + c * kBlockN * 128, &p.tma_v, &v_full[s], col0 + 32 * c, vrow);
+          ++issued_v;
+        }
       }
+      // No TMA may still be writing this CTA's shared memory at exit.
       mbar_wait(&q_full, 0, nullptr, 0);
-      for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, 0);
+      for (int j = max(0, issued_k - 2); j < issued_k; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, nullptr, 0);
+      for (int j = max(0, issued_v - 2); j < issued_v; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1, nullptr, 0);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
@@ -235,7 +262,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
       // S_j = Q K_j^T into SP[j & 1].
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait(PASSES == 3 ? &kv_conv[s] : &kv_full[s], (j >> 1) & 1, p.status, kStatusTimeoutFull))
+        if (!mbar_wait(PASSES == 3 ? &k_conv[s] : &k_full[s], (j >> 1) & 1, p.status, kStatusTimeoutFull))
           return false;
         ABACUS_FWD_TRACE(2, j)
         tc_fence_after();
@@ -259,6 +286,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
           }
         }
         mma_commit(&s_full[s]);
+        mma_commit(&k_empty[s]);
         return true;
       };
       // PV_j = P_j V_j into PV[j & 1].
@@ -266,6 +294,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
         const int s = j & 1;
         if (!mbar_wait(&p_full[s], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) return false;
         if (j >= 2 && !mbar_wait(&pv_empty[s], ((j >> 1) - 1) & 1, p.status, kStatusTimeoutAccum)) return false;
+        if (!mbar_wait(PASSES == 3 ? &v_conv[s] : &v_full[s], (j >> 1) & 1, p.status, kStatusTimeoutFull)) return false;
         ABACUS_FWD_TRACE(3, j)
         tc_fence_after();
         const uint32_t d = tmem + Cfg::kPVBase + s * D;
@@ -285,7 +314,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
           }
         }
         mma_commit(&pv_full[s]);
-        mma_commit(&kv_empty[s]);
+        mma_commit(&v_empty[s]);
         return true;
       };
       for (int j = 0; j < nb && ok; ++j) {
@@ -295,7 +324,10 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
       if (ok && nb >= 1) ok = issue_pv(nb - 1);
       // Drain: every commit lands before this CTA releases its shared memory.
       if (nb >= 1) {
-        for (int j = max(0, nb - 2); j < nb; ++j) mbar_wait(&kv_empty[j & 1], (j >> 1) & 1, p.status, kStatusTimeoutEmpty);
+        for (int j = max(0, nb - 2); j < nb; ++j) {
+          mbar_wait(&k_empty[j & 1], (j >> 1) & 1, p.status, kStatusTimeoutEmpty);
+          mbar_wait(&v_empty[j & 1], (j >> 1) & 1, p.status, kStatusTimeoutEmpty);
+        }
       }
     }
   } else if (warp < 6) {
@@ -349,7 +381,7 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
           for (int i = 0; i < 32; ++i) bmax = fmaxf(bmax, sv[i]);
         }
         const float m_new = fmaxf(m, bmax);
-        alpha = (m == -FLT_MAX) ? 0.f : fast_exp2(m - m_new);
+        alpha = (m == -FLT_MAX) ? 0.f : ex2_approx(m - m_new);
         float bsum = 0.f;
         // P into the TMEM columns S came from (and the next kBlockN for P lo).
 #pragma unroll
@@ -360,12 +392,12 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
           uint32_t vl[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float e = (sv[i] == -FLT_MAX) ? 0.f : fast_exp2(sv[i] - m_new);
+            const float e = (sv[i] == -FLT_MAX) ? 0.f : ex2_approx(sv[i] - m_new);
             bsum += e;
             if (PASSES == 3) {
-              const float hi = to_tf32(e);
+              const float hi = to_tf32_alu(e);
               vh[i] = __float_as_uint(hi);
-              vl[i] = __float_as_uint(to_tf32(e - hi));
+              vl[i] = __float_as_uint(to_tf32_alu(e - hi));
             } else {
               vh[i] = __float_as_uint(e);
             }
@@ -430,14 +462,23 @@ __global__ void __launch_bounds__(FwdCfg<D, PASSES>::kThreads, 1) flash_fwd_kern
       fence_proxy_async_smem();
       mbar_arrive(&q_conv);
     }
-    for (int j = 0; j < nb && ok; ++j) {
-      const int s = j & 1;
-      if (!mbar_wait_warp(&kv_full[s], (j >> 1) & 1, p.status, kStatusTimeoutFull)) break;
-      split(k_hi(s), k_lo(s), Cfg::kKBytes);
-      split(v_hi(s), v_lo(s), Cfg::kVBytes);
-      fence_proxy_async_smem();
-      mbar_arrive(&kv_conv[s]);
-      if (ct == 0) ABACUS_FWD_TRACE(1, j)
+    // Same order as the producer: K_j, then V_{j-1}.
+    for (int j = 0; j <= nb && ok; ++j) {
+      if (j < nb) {
+        const int s = j & 1;
+        if (!mbar_wait_warp(&k_full[s], (j >> 1) & 1, p.status, kStatusTimeoutFull)) break;
+        split(k_hi(s), k_lo(s), Cfg::kKBytes);
+        fence_proxy_async_smem();
+        mbar_arrive(&k_conv[s]);
+        if (ct == 0) ABACUS_FWD_TRACE(1, j)
+      }
+      if (j >= 1) {
+        const int s = (j - 1) & 1;
+        if (!mbar_wait_warp(&v_full[s], ((j - 1) >> 1) & 1, p.status, kStatusTimeoutFull)) break;
+        split(v_hi(s), v_lo(s), Cfg::kVBytes);
+        fence_proxy_async_smem();
+        mbar_arrive(&v_conv[s]);
+      }
     }
   }
 

@@ -325,6 +325,29 @@ __device__ __forceinline__ float to_tf32(float x) {
   return __uint_as_float(r);
 }
 
+// The same rounding (to nearest, ties away from zero, onto 10 explicit
+// mantissa bits) on the integer ALUs: adding half a tf32 ulp (bit 12) to the
+// magnitude bits carries into bit 13 exactly when the 13 dropped bits are at
+// least half an ulp (a carry out of the mantissa bumps the exponent, which is
+// the correctly rounded value), then the dropped bits are cleared. Infinities
+// and NaNs (all exponent bits set) pass through unchanged. Used in the
+// attention softmax loops, where the conversion would otherwise queue behind
+// the exponentials; measured slower than the conversion instruction in the
+// GEMM split converter, which therefore keeps to_tf32.
+__device__ __forceinline__ float to_tf32_alu(float x) {
+  const uint32_t u = __float_as_uint(x);
+  const uint32_t r = (u + 0x1000u) & 0xffffe000u;
+  return __uint_as_float((u & 0x7f800000u) == 0x7f800000u ? u : r);
+}
+
+// 2^x on the special-function unit (ex2.approx, denormal results flushed to
+// zero). Softmax probabilities below 2^-126 are zero for training purposes.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // The value a kind::tf32 MMA uses for an fp32 operand element read from shared
 // memory or TMEM: the low 13 mantissa bits dropped (measured on B200). An
 // operand left as raw fp32 therefore acts as its own "hi" part, and only

@@ -37,6 +37,7 @@ from abacus_b200.parallel.pipeline_parallel import (
     shifted_targets,
 )
 from abacus_b200.utils.dist import print_peak_memory
+from abacus_b200.utils.trace import PhaseTracer
 
 IGNORE = -100
 
@@ -63,6 +64,7 @@ class Trainer:
         schedule_lr: float = 5e-4,
         print_memory: bool = False,
         device: torch.device | str | None = None,
+        tracer: PhaseTracer | None = None,
     ):
         if parallel is not None and pipeline is not None and mesh.get_mesh() is None:
             raise ValueError("pipeline parallel does not use DataParallel")
@@ -73,6 +75,8 @@ class Trainer:
         self.parallel = parallel
         self.pipeline = pipeline
         self.print_memory = print_memory
+        # NVTX range (and optional device timing) per phase of a step.
+        self.tracer = tracer if tracer is not None else PhaseTracer()
         owned = grad_shards = None
         if parallel is not None:
             parallel.broadcast_parameters()
@@ -95,30 +99,35 @@ class Trainer:
     def step(self, tokens_BL: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         self.model.train()
         tokens_BL = tokens_BL.to(self.device, non_blocking=True)
+        phase = self.tracer.phase
         if self.pipeline is not None:
             self.optimizer.zero_grad()
-            loss = self.pipeline.forward_backward(tokens_BL).detach()
+            with phase("pipeline_forward_backward", self.device):
+                loss = self.pipeline.forward_backward(tokens_BL).detach()
             if getattr(self.model, "context_parallel", False) and mesh.rank_and_world_size("cp")[1] > 1:
-                sum_parameter_gradients(self.model)
-                # Each CP rank of the last stage holds its shard's share of the loss.
-                loss = loss.clone()
-                dist.all_reduce(loss, op=dist.ReduceOp.SUM, group=mesh.group_for("cp"))
-            self._optimizer_step()
+                with phase("cp_sync", self.device):
+                    sum_parameter_gradients(self.model)
+                    # Each CP rank of the last stage holds its shard's share of the loss.
+                    loss = loss.clone()
+                    dist.all_reduce(loss, op=dist.ReduceOp.SUM, group=mesh.group_for("cp"))
+            with phase("optimizer", self.device):
+                self._optimizer_step()
             return loss, loss
         inputs_BL = tokens_BL.clamp(min=0)  # -100 is padding; the embedding has no row for it
         if self._context_parallel_active():
             return self._context_parallel_step(tokens_BL, inputs_BL)
-        targets = shifted_targets(tokens_BL)
-        token_count = (targets != IGNORE).sum()
-        if not tokens_BL.is_cuda and int(token_count) < 1:
-            raise ValueError("batch has no target tokens")
-        normalizer = token_count.to(torch.float32)
-        if self.parallel is not None and not self.parallel.token_weighted:
-            # Loss divided by the global token count; gradients are then summed.
-            normalizer = normalizer.clone()
-            dist.all_reduce(normalizer, op=dist.ReduceOp.SUM, group=self.parallel.group)
-        loss = self.model(inputs_BL, targets=targets, normalizer=normalizer)
-        loss = self._with_aux_loss(loss)
+        with phase("forward", self.device):
+            targets = shifted_targets(tokens_BL)
+            token_count = (targets != IGNORE).sum()
+            if not tokens_BL.is_cuda and int(token_count) < 1:
+                raise ValueError("batch has no target tokens")
+            normalizer = token_count.to(torch.float32)
+            if self.parallel is not None and not self.parallel.token_weighted:
+                # Loss divided by the global token count; gradients are then summed.
+                normalizer = normalizer.clone()
+                dist.all_reduce(normalizer, op=dist.ReduceOp.SUM, group=self.parallel.group)
+            loss = self.model(inputs_BL, targets=targets, normalizer=normalizer)
+            loss = self._with_aux_loss(loss)
         self.optimizer.zero_grad()
         if self.print_memory:
             print_peak_memory()
@@ -130,14 +139,18 @@ class Trainer:
             # token count are fixed before backward.
             self._advance_lr()
             self.parallel.prepare_step(self.optimizer, token_count)
-        loss.backward()
+        with phase("backward", self.device):
+            loss.backward()
         local_loss = loss.detach()
         if self.parallel is not None:
-            loss = self.parallel.synchronize(loss, token_count)
+            with phase("dp_sync", self.device):
+                loss = self.parallel.synchronize(loss, token_count)
         if not self._fused:
-            self._optimizer_step()
+            with phase("optimizer", self.device):
+                self._optimizer_step()
         if self.parallel is not None:
-            self.parallel.gather_parameters()
+            with phase("dp_gather", self.device):
+                self.parallel.gather_parameters()
         return loss.detach(), local_loss
 
     def _with_aux_loss(self, loss):
@@ -166,22 +179,27 @@ class Trainer:
     def _context_parallel_step(self, tokens_BL, inputs_BL):
         """Global token-weighted loss across CP ranks (``abacus/trainer.py:115-148``);
         parameter gradients are summed over the CP group after backward."""
+        phase = self.tracer.phase
         rank, world = mesh.rank_and_world_size("cp")
         group = mesh.group_for("cp")
-        targets = context_parallel_targets(tokens_BL, rank, world)
-        local_count = (targets != IGNORE).sum()
-        total_count = local_count.to(torch.float32)
-        dist.all_reduce(total_count, op=dist.ReduceOp.SUM, group=group)
-        if not tokens_BL.is_cuda and total_count.item() < 1:
-            raise ValueError("batch has no target tokens")
-        loss = self.model(inputs_BL, targets=targets, normalizer=total_count)
-        local_sum = loss.detach() * total_count
+        with phase("forward", self.device):
+            targets = context_parallel_targets(tokens_BL, rank, world)
+            local_count = (targets != IGNORE).sum()
+            total_count = local_count.to(torch.float32)
+            dist.all_reduce(total_count, op=dist.ReduceOp.SUM, group=group)
+            if not tokens_BL.is_cuda and total_count.item() < 1:
+                raise ValueError("batch has no target tokens")
+            loss = self.model(inputs_BL, targets=targets, normalizer=total_count)
+            local_sum = loss.detach() * total_count
         self.optimizer.zero_grad()
         if self.print_memory:
             print_peak_memory()
-        loss.backward()
-        sum_parameter_gradients(self.model)
-        self._optimizer_step()
+        with phase("backward", self.device):
+            loss.backward()
+        with phase("cp_sync", self.device):
+            sum_parameter_gradients(self.model)
+        with phase("optimizer", self.device):
+            self._optimizer_step()
         reported = local_sum.clone()
         dist.all_reduce(reported, op=dist.ReduceOp.SUM, group=group)
         global_loss = (reported / total_count).detach()

@@ -34,6 +34,8 @@ def base_parser(description: str) -> argparse.ArgumentParser:
     p.add_argument("--vocab-size", type=int, default=50304, help="vocabulary of synthetic data")
     p.add_argument("--precision", choices=("fp32", "tf32"), default="fp32")
     p.add_argument("--steps", type=int, default=None)
+    p.add_argument("--phase-times", action="store_true",
+                   help="print device time per step phase (forward / backward / sync / optimizer) and tokens/s")
     return p
 
 
@@ -77,6 +79,14 @@ def run_loop(trainer, batches, total_steps, device, distributed, log_every: int 
         elif is_main and step % log_every == 0:
             print(f"step {step}/{total_steps} loss {loss.item():.4f} batch {tokens.shape[0]} length {tokens.shape[1]}",
                   flush=True)
+        tracer = getattr(trainer, "tracer", None)
+        if tracer is not None and tracer.timing:
+            times = tracer.times_ms()
+            if is_main and step % log_every == 0:
+                total = sum(times.values())
+                rate = tokens.numel() / (total / 1e3) if total > 0 else 0.0
+                parts = " ".join(f"{k} {v:.1f} ms" for k, v in times.items())
+                print(f"  phases: {parts} | {rate:,.0f} tokens/s on this rank", flush=True)
     if is_main:
         print(f"Execution time {time.perf_counter() - started:.1f}", flush=True)
 

@@ -12,6 +12,7 @@ import torch  # noqa: E402
 
 from abacus_b200.model_config import DIM, HEAD_DIM, N_BLOCKS, N_HEADS  # noqa: E402
 from abacus_b200.trainer import Trainer  # noqa: E402
+from abacus_b200.utils.trace import PhaseTracer  # noqa: E402
 from abacus_b200.transformer import Transformer  # noqa: E402
 from abacus_b200.utils import cli  # noqa: E402
 
@@ -28,7 +29,7 @@ def main():
         torch.manual_seed(0)
         model = Transformer(dim=DIM, n_heads=N_HEADS, head_dim=HEAD_DIM, n_blocks=N_BLOCKS, vocab_size=vocab,
                             context_parallel=True).to(device)
-        trainer = Trainer(model, total_steps=total_steps)
+        trainer = Trainer(model, total_steps=total_steps, tracer=PhaseTracer(timing=args.phase_times))
         batches = cli.padded_batches(docs, args.batch, multiple_of=2 * world)
         cli.run_loop(trainer, batches, total_steps, device, distributed, max_steps=args.steps)
     finally:

@@ -15,6 +15,7 @@ import torch.distributed as dist  # noqa: E402
 
 from abacus_b200.distributed.data_parallel import DataParallel  # noqa: E402
 from abacus_b200.trainer import Trainer  # noqa: E402
+from abacus_b200.utils.trace import PhaseTracer  # noqa: E402
 from abacus_b200.transformer import Transformer  # noqa: E402
 from abacus_b200.utils import cli  # noqa: E402
 
@@ -49,7 +50,7 @@ def main():
         model = Transformer(dim=cfg["dim"], n_heads=cfg["n_heads"], head_dim=cfg["head_dim"], n_blocks=cfg["n_blocks"],
                             vocab_size=vocab, hidden_dim=cfg["hidden_dim"]).to(device)
         parallel = DataParallel(model, stage=args.zero) if distributed else None
-        trainer = Trainer(model, parallel, total_steps=total_steps)
+        trainer = Trainer(model, parallel, total_steps=total_steps, tracer=PhaseTracer(timing=args.phase_times))
         if args.wandb and rank_ == 0:
             import wandb
 

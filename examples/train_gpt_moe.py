@@ -18,6 +18,7 @@ from abacus_b200.distributed.data_parallel import DataParallel  # noqa: E402
 from abacus_b200.model_config import DIM, HEAD_DIM, N_BLOCKS, N_HEADS  # noqa: E402
 from abacus_b200.parallel import mesh  # noqa: E402
 from abacus_b200.trainer import Trainer  # noqa: E402
+from abacus_b200.utils.trace import PhaseTracer  # noqa: E402
 from abacus_b200.transformer_moe import TransformerMoe  # noqa: E402
 from abacus_b200.utils import cli  # noqa: E402
 
@@ -53,7 +54,7 @@ def main():
         if edp:
             expert_params = [p for n, p in model.named_parameters() if ".moe.w_" in n]
             parallel = DataParallel(model, exclude=expert_params, token_weighted=False)
-        trainer = Trainer(model, parallel, total_steps=total_steps)
+        trainer = Trainer(model, parallel, total_steps=total_steps, tracer=PhaseTracer(timing=args.phase_times))
         cli.run_loop(trainer, cli.padded_batches(docs, args.batch), total_steps, device, distributed,
                      max_steps=args.steps)
     finally:

@@ -15,6 +15,7 @@ import torch  # noqa: E402
 from abacus_b200.distributed.pipeline_parallel import PipelineParallel  # noqa: E402
 from abacus_b200.parallel import mesh  # noqa: E402
 from abacus_b200.trainer import Trainer  # noqa: E402
+from abacus_b200.utils.trace import PhaseTracer  # noqa: E402
 from abacus_b200.transformer import PipelineStage  # noqa: E402
 from abacus_b200.utils import cli  # noqa: E402
 
@@ -43,7 +44,7 @@ def main():
         stage = PipelineStage(args.dim, args.heads, args.head_dim, args.blocks, vocab, rank=c["pp"], world_size=m.pp,
                               hidden_dim=args.hidden, context_parallel=args.cp > 1).to(device)
         trainer = Trainer(stage, pipeline=PipelineParallel(stage, n_microbatches=args.microbatches),
-                          total_steps=total_steps)
+                          total_steps=total_steps, tracer=PhaseTracer(timing=args.phase_times))
         batches = cli.padded_batches(docs, args.batch, multiple_of=2 * args.cp)
 
         def on_step(step, loss, local, tokens):

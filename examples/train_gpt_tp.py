@@ -16,6 +16,7 @@ import torch  # noqa: E402
 from abacus_b200.distributed.data_parallel import DataParallel  # noqa: E402
 from abacus_b200.parallel import mesh  # noqa: E402
 from abacus_b200.trainer import Trainer  # noqa: E402
+from abacus_b200.utils.trace import PhaseTracer  # noqa: E402
 from abacus_b200.transformer import Transformer  # noqa: E402
 from abacus_b200.utils import cli  # noqa: E402
 
@@ -45,7 +46,7 @@ def main():
                             vocab_size=vocab, hidden_dim=args.hidden, tensor_parallel=True,
                             sequence_parallel=args.sequence_parallel).to(device)
         parallel = DataParallel(model) if args.dp > 1 else None
-        trainer = Trainer(model, parallel, total_steps=total_steps)
+        trainer = Trainer(model, parallel, total_steps=total_steps, tracer=PhaseTracer(timing=args.phase_times))
         tp = m.tp if m else 1
         multiple = tp if args.sequence_parallel else 1
         cli.run_loop(trainer, cli.padded_batches(docs, args.batch, multiple_of=multiple), total_steps, device,

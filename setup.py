@@ -24,8 +24,6 @@ sources = sorted(
     glob.glob(os.path.join(CSRC, "**", "*.cu"), recursive=True)
     + glob.glob(os.path.join(CSRC, "**", "*.cpp"), recursive=True)
 )
-# Stand-alone C-ABI libraries are built separately (abacus_b200/native.py).
-sources = [s for s in sources if "/capi/" not in s]
 
 NVCC_FLAGS = [
     "-gencode=arch=compute_100a,code=sm_100a",

@@ -85,6 +85,7 @@ void tp_reduce_rows(torch::Tensor staging, int64_t world, torch::Tensor counters
 void ep_push_rows(torch::Tensor src, int64_t top_k, torch::Tensor dest_rank, torch::Tensor dest_row,
                   c10::optional<torch::Tensor> scale, std::vector<int64_t> row_ptrs, std::vector<int64_t> meta_ptrs,
                   std::vector<int64_t> flag_ptrs, int64_t self, int64_t epoch, torch::Tensor done);
+void ep_credit(torch::Tensor counter, torch::Tensor amount, int64_t multiplier);
 void ep_combine(torch::Tensor ret, c10::optional<torch::Tensor> weights, int64_t top_k, torch::Tensor counter,
                 int64_t target, torch::Tensor out);
 void ar_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, torch::Tensor counts, bool normalize,

@@ -47,6 +47,7 @@ void launch_fwd(const FwdParams& p, dim3 grid, cudaStream_t s) {
 
 // Optional phase trace of the forward kernel (debugging / profiling aid).
 long long* g_fwd_trace = nullptr;
+long long* g_bwd_trace = nullptr;
 
 const int64_t* positions_ptr(const c10::optional<torch::Tensor>& pos, int64_t len, const char* name) {
   if (!pos) return nullptr;
@@ -74,11 +75,13 @@ void flash_bwd_impl(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
 void flash_fwd_trace(c10::optional<torch::Tensor> buf) {
   if (!buf) {
     g_fwd_trace = nullptr;
+    g_bwd_trace = nullptr;
     return;
   }
-  TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == torch::kInt64 && buf->is_contiguous() && buf->numel() >= 9 * 64,
-              "trace buffer: contiguous int64 CUDA tensor of >= 576 entries");
+  TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == torch::kInt64 && buf->is_contiguous() && buf->numel() >= 14 * 64,
+              "trace buffer: contiguous int64 CUDA tensor of >= 896 entries");
   g_fwd_trace = reinterpret_cast<long long*>(buf->data_ptr<int64_t>());
+  g_bwd_trace = g_fwd_trace + 9 * 64;  // the dK/dV kernel's stamps follow
 }
 
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
@@ -295,6 +298,7 @@ void flash_bwd_impl(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
   p.scale = static_cast<float>(scale);
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.status = host::status_ptr(q.device().index());
+  p.trace = g_bwd_trace;
   if (!scatter.empty()) {
     const size_t world = (scatter.size() - 1) / 3;
     TORCH_CHECK(world >= 1 && world <= 8, "scatter over 1..8 ranks");

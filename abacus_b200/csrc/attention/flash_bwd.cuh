@@ -57,6 +57,10 @@ struct BwdParams {
   unsigned* scatter_counter[8];
   int scatter_chunk;
   int* status;
+  // Optional phase trace of the dK/dV kernel (clock64 stamps of CTA (0, 0, 0),
+  // slot * 64 + block): 0 S^T / dP^T issued, 1 S^T seen by the threads,
+  // 2 P^T / dS^T written, 3 dV / dK issued, 4 partials drained.
+  long long* trace;
 };
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -139,21 +143,28 @@ struct DkdvCfg {
   static constexpr int kKVTile = kOuter * D * 4;         // K or V
   static constexpr int kQTile = kInner * D * 4;          // one layout of Q or dO
   static constexpr int kStageBytes = 4 * kQTile * kSplit;  // Q_k, Q_mn, dO_k, dO_mn [+ lo]
-  static constexpr int kSmemBytes = 2 * kKVTile * kSplit + kStageBytes + 1024;
+  static constexpr int kSmemRaw = 2 * kKVTile * kSplit + kStageBytes + 1024;
   static constexpr int kThreads = PASSES == 3 ? 320 : 192;
   // Register cap for one CTA per SM: each of the 4 SM sub-partitions holds
   // 16384 registers and ceil(warps / 4) of the CTA's warps.
   static constexpr int kWarpsPerSubpartition = (kThreads / 32 + 3) / 4;
   static constexpr int kMaxRegs =
       (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8 > 255 ? 255 : (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8;
-  // TMEM: ST (S^T, P^T hi [, P^T lo]), DPT (dP^T, dS^T hi [, dS^T lo]),
-  // dV, dK partials [+ dV, dK masters in 3xTF32 mode].
+  // TMEM: two buffers (blocks alternate) of ST (S^T, P^T hi [, P^T lo]) and
+  // DPT (dP^T, dS^T hi [, dS^T lo]), so the next block's score MMAs run while
+  // the threads turn this block's scores into P^T / dS^T; then the dV, dK
+  // partials [+ dV, dK masters in 3xTF32 mode].
   static constexpr int kSTCols = kInner * kSplit;
-  static constexpr int kST = 0, kDPT = kSTCols, kDVp = 2 * kSTCols, kDKp = kDVp + D;
+  static constexpr int kST = 0, kDPT = kSTCols, kBufCols = 2 * kSTCols;
+  static constexpr int kDVp = 2 * kBufCols, kDKp = kDVp + D;
   static constexpr int kDVm = kDKp + D, kDKm = kDVm + D;
   static constexpr int kCols = PASSES == 3 ? kDKm + D : kDKp + D;
   static constexpr uint32_t kTmemCols = kCols <= 256 ? 256 : 512;
   static constexpr int kMaxBlocks = 2048;
+  // A CTA that takes all 512 TMEM columns must be alone on its SM (a second
+  // one would wait in tcgen05.alloc for the first to finish): ask for more
+  // than half of the SM's shared memory.
+  static constexpr int kSmemBytes = (kTmemCols == 512 && kSmemRaw < 116 * 1024) ? 116 * 1024 : kSmemRaw;
 };
 
 template <int D, int PASSES>
@@ -165,7 +176,7 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
   // Q / dO tiles come in two groups with their own barriers: the K-major
   // tiles (S^T, dP^T MMAs) and the MN-major tiles (dV, dK MMAs), so the next
   // block's K-major tiles load while this block's threads and dV / dK MMAs run.
-  __shared__ uint64_t kv_full, kv_conv, st_full, p_full, part_full;
+  __shared__ uint64_t kv_full, kv_conv, st_full[2], p_full[2], part_full;
   __shared__ uint64_t kf_full, kf_conv, kf_empty, mn_full, mn_conv, mn_empty;
   __shared__ uint32_t tmem_slot;
   __shared__ int n_blocks;
@@ -173,6 +184,9 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
   __shared__ int block_list[Cfg::kMaxBlocks];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const bool traced = p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+#define ABACUS_BWD_TRACE(slot, i) \
+  if (traced && (i) < 64) p.trace[(slot) * 64 + (i)] = clock64();
   if (threadIdx.x == 0) abort_flag = *reinterpret_cast<volatile int*>(p.status);
   __syncthreads();
   if (abort_flag != kStatusOk) return;
@@ -195,8 +209,10 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
   if (threadIdx.x == 0) {
     mbar_init(&kv_full, 1);
     mbar_init(&kv_conv, 128);
-    mbar_init(&st_full, 1);
-    mbar_init(&p_full, 128);
+    mbar_init(&st_full[0], 1);
+    mbar_init(&st_full[1], 1);
+    mbar_init(&p_full[0], 128);
+    mbar_init(&p_full[1], 128);
     mbar_init(&part_full, 1);
     mbar_init(&kf_full, 1);
     mbar_init(&kf_conv, 128);
@@ -226,27 +242,35 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
         tma_load_2d(sk + c * 128 * 128, &p.tma_k_k, &kv_full, col0 + 32 * c, k_row0);
         tma_load_2d(sv + c * 128 * 128, &p.tma_v_k, &kv_full, col0 + 32 * c, k_row0);
       }
+      // The K-major tiles run one block ahead of the MN-major ones: block
+      // i+1's score MMAs are issued before block i's gradient MMAs.
       int issued_k = 0, issued_mn = 0;
-      for (int i = 0; i < nb; ++i) {
-        const int qrow = q_row_base + (block_list[i] & 0xFFFF) * NQ;
-        // K-major Q / dO: free once the previous block's S^T / dP^T MMAs ran.
-        if (i >= 1 && !mbar_wait(&kf_empty, (i - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&kf_full, 2 * Cfg::kQTile);
+      for (int step = 0; step <= nb; ++step) {
+        if (step < nb) {
+          const int qrow = q_row_base + (block_list[step] & 0xFFFF) * NQ;
+          // K-major Q / dO: free once the previous block's S^T / dP^T MMAs ran.
+          if (step >= 1 && !mbar_wait(&kf_empty, (step - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+          mbar_arrive_expect_tx(&kf_full, 2 * Cfg::kQTile);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          tma_load_2d(tile(0, 0) + c * NQ * 128, &p.tma_q_k, &kf_full, col0 + 32 * c, qrow);
-          tma_load_2d(tile(2, 0) + c * NQ * 128, &p.tma_do_k, &kf_full, col0 + 32 * c, qrow);
+          for (int c = 0; c < D / 32; ++c) {
+            tma_load_2d(tile(0, 0) + c * NQ * 128, &p.tma_q_k, &kf_full, col0 + 32 * c, qrow);
+            tma_load_2d(tile(2, 0) + c * NQ * 128, &p.tma_do_k, &kf_full, col0 + 32 * c, qrow);
+          }
+          ++issued_k;
         }
-        ++issued_k;
-        // MN-major Q / dO: free once the previous block's dV / dK MMAs ran.
-        if (i >= 1 && !mbar_wait(&mn_empty, (i - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&mn_full, 2 * Cfg::kQTile);
+        if (step >= 1) {
+          const int i = step - 1;
+          const int qrow = q_row_base + (block_list[i] & 0xFFFF) * NQ;
+          // MN-major Q / dO: free once the previous block's dV / dK MMAs ran.
+          if (i >= 1 && !mbar_wait(&mn_empty, (i - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+          mbar_arrive_expect_tx(&mn_full, 2 * Cfg::kQTile);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          tma_load_2d(tile(1, 0) + c * NQ * 128, &p.tma_q_mn, &mn_full, col0 + 32 * c, qrow);
-          tma_load_2d(tile(3, 0) + c * NQ * 128, &p.tma_do_mn, &mn_full, col0 + 32 * c, qrow);
+          for (int c = 0; c < D / 32; ++c) {
+            tma_load_2d(tile(1, 0) + c * NQ * 128, &p.tma_q_mn, &mn_full, col0 + 32 * c, qrow);
+            tma_load_2d(tile(3, 0) + c * NQ * 128, &p.tma_do_mn, &mn_full, col0 + 32 * c, qrow);
+          }
+          ++issued_mn;
         }
-        ++issued_mn;
       }
       mbar_wait(&kv_full, 0, nullptr, 0);
       if (issued_k > 0) mbar_wait(&kf_full, (issued_k - 1) & 1, nullptr, 0);
@@ -258,16 +282,17 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
       constexpr uint32_t idesc_s = idesc_tf32(128, NQ, false, false);
       constexpr uint32_t idesc_acc = idesc_tf32(128, D, false, true);
       bool ok = mbar_wait(PASSES == 3 ? &kv_conv : &kv_full, 0, p.status, kStatusTimeoutFull);
-      for (int i = 0; i < nb && ok; ++i) {
-        if (!mbar_wait(PASSES == 3 ? &kf_conv : &kf_full, i & 1, p.status, kStatusTimeoutFull)) break;
+      // S^T = K Q^T and dP^T = V dO^T of block i into TMEM buffer i & 1.
+      auto issue_scores = [&](int i) -> bool {
+        if (!mbar_wait(PASSES == 3 ? &kf_conv : &kf_full, i & 1, p.status, kStatusTimeoutFull)) return false;
         tc_fence_after();
-        // S^T = K Q^T and dP^T = V dO^T.
+        const int buf = (i & 1) * Cfg::kBufCols;
 #pragma unroll
         for (int pair = 0; pair < 2; ++pair) {
           const uint32_t a_hi = smem_u32(pair == 0 ? sk : sv);
           const uint32_t b_hi = smem_u32(tile(pair == 0 ? 0 : 2, 0));
           const uint32_t b_lo = smem_u32(tile(pair == 0 ? 0 : 2, 1));
-          const uint32_t d = tmem + (pair == 0 ? Cfg::kST : Cfg::kDPT);
+          const uint32_t d = tmem + buf + (pair == 0 ? Cfg::kST : Cfg::kDPT);
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
 #pragma unroll
@@ -285,24 +310,30 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
             }
           }
         }
-        mma_commit(&st_full);
+        ABACUS_BWD_TRACE(0, i)
+        mma_commit(&st_full[i & 1]);
         mma_commit(&kf_empty);
-        if (!mbar_wait(&p_full, i & 1, p.status, kStatusTimeoutAccum)) break;
-        if (!mbar_wait(PASSES == 3 ? &mn_conv : &mn_full, i & 1, p.status, kStatusTimeoutFull)) break;
+        return true;
+      };
+      // dV (+)= P^T dO and dK (+)= dS^T Q of block i, A from TMEM buffer i & 1.
+      // 3xTF32: the tensor core accumulates two consecutive blocks (a 64-deep
+      // reduction, as in the GEMM) before the threads fold the partial into
+      // the fp32 masters; tf32: everything accumulates in TMEM.
+      auto issue_grads = [&](int i) -> bool {
+        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1, p.status, kStatusTimeoutAccum)) return false;
+        if (!mbar_wait(PASSES == 3 ? &mn_conv : &mn_full, i & 1, p.status, kStatusTimeoutFull)) return false;
         tc_fence_after();
-        // dV (+)= P^T dO and dK (+)= dS^T Q.
+        const int buf = (i & 1) * Cfg::kBufCols;
 #pragma unroll
         for (int pair = 0; pair < 2; ++pair) {
-          const uint32_t a = tmem + (pair == 0 ? Cfg::kST : Cfg::kDPT);
+          const uint32_t a = tmem + buf + (pair == 0 ? Cfg::kST : Cfg::kDPT);
           const uint32_t bh = smem_u32(tile(pair == 0 ? 3 : 1, 0));
           const uint32_t bl = smem_u32(tile(pair == 0 ? 3 : 1, 1));
           const uint32_t d = tmem + (pair == 0 ? Cfg::kDVp : Cfg::kDKp);
 #pragma unroll
           for (int ks = 0; ks < NQ / 8; ++ks) {
             const uint64_t vb = desc_mnmajor_sw128_32b(bh + ks * 1024, NQ * 128);
-            // 3xTF32: a fresh partial per block (drained by the threads);
-            // tf32: accumulate over all blocks in TMEM.
-            const uint32_t acc = PASSES == 3 ? (ks ? 1u : 0u) : ((i | ks) ? 1u : 0u);
+            const uint32_t acc = PASSES == 3 ? ((ks | (i & 1)) ? 1u : 0u) : ((i | ks) ? 1u : 0u);
             if (PASSES == 3) {
               const uint64_t vl = desc_mnmajor_sw128_32b(bl + ks * 1024, NQ * 128);
               mma_tf32_ts(d, a + NQ + ks * 8, vb, idesc_acc, acc);
@@ -313,8 +344,17 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
             }
           }
         }
+        ABACUS_BWD_TRACE(3, i)
         mma_commit(&part_full);
         mma_commit(&mn_empty);
+        return true;
+      };
+      if (ok && nb > 0) ok = issue_scores(0);
+      for (int i = 0; i < nb && ok; ++i) {
+        // The next block's scores go ahead of this block's gradient MMAs; its
+        // buffer was last read by block i - 1's gradient MMAs, issued earlier.
+        if (i + 1 < nb) ok = issue_scores(i + 1);
+        if (ok) ok = issue_grads(i);
       }
       if (nb > 0) {
         mbar_wait(&kf_empty, (nb - 1) & 1, p.status, kStatusTimeoutEmpty);
@@ -331,10 +371,10 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
     const float* lse_bh = p.lse + (static_cast<long long>(b) * p.heads + h) * p.lq;
     const float* delta_bh = p.delta + (static_cast<long long>(b) * p.heads + h) * p.lq;
     bool ok = true;
-    // Add the previous block's partials into the TMEM masters (3xTF32 only).
-    auto drain = [&](int i) -> bool {
-      if (!mbar_wait_warp(&part_full, i & 1, p.status, kStatusTimeoutAccum)) return false;
-      tc_fence_after();
+    // 3xTF32: add the dV / dK partial (one or two blocks, see the MMA
+    // issuer) into the fp32 TMEM masters; the first fold initialises them.
+    bool have_master = false;
+    auto fold = [&](int i) {
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const int part = which == 0 ? Cfg::kDVp : Cfg::kDKp;
@@ -343,21 +383,22 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
         for (int c = 0; c < D / 32; ++c) {
           uint32_t a[32], m[32];
           tmem_ld32(lb + part + c * 32, a);
-          if (i > 0) tmem_ld32(lb + master + c * 32, m);
+          if (have_master) tmem_ld32(lb + master + c * 32, m);
           tmem_ld_wait();
 #pragma unroll
           for (int t = 0; t < 32; ++t)
-            m[t] = __float_as_uint((i > 0 ? __uint_as_float(m[t]) : 0.f) + __uint_as_float(a[t]));
+            m[t] = __float_as_uint((have_master ? __uint_as_float(m[t]) : 0.f) + __uint_as_float(a[t]));
           tmem_st32(lb + master + c * 32, m);
         }
       }
-      tmem_st_wait();
-      return true;
+      have_master = true;
+      if (threadIdx.x == 64) ABACUS_BWD_TRACE(4, i)
     };
     for (int i = 0; i < nb && ok; ++i) {
       const int entry = block_list[i];
       const int qb = entry & 0xFFFF;
       const bool partial = (entry >> 30) & 1;
+      const int buf = (i & 1) * Cfg::kBufCols;
       // This block's lse / Delta / query positions, one query per lane, loaded
       // before the wait for S^T so their latency hides behind it; the row loop
       // below broadcasts them with shuffles.
@@ -371,16 +412,17 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
         dl_l[c] = __ldg(delta_bh + qc);
         qpos_l[c] = qi < p.lq ? (p.q_pos ? static_cast<int>(__ldg(p.q_pos + qi)) : qi) : INT_MIN;
       }
-      if (!mbar_wait_warp(&st_full, i & 1, p.status, kStatusTimeoutAccum)) {
+      if (!mbar_wait_warp(&st_full[i & 1], (i >> 1) & 1, p.status, kStatusTimeoutAccum)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      if (threadIdx.x == 64) ABACUS_BWD_TRACE(1, i)
 #pragma unroll
       for (int c = 0; c < NQ / 32; ++c) {
         uint32_t sv32[32], dp32[32];
-        tmem_ld32(lb + Cfg::kST + c * 32, sv32);
-        tmem_ld32(lb + Cfg::kDPT + c * 32, dp32);
+        tmem_ld32(lb + buf + Cfg::kST + c * 32, sv32);
+        tmem_ld32(lb + buf + Cfg::kDPT + c * 32, dp32);
         tmem_ld_wait();
         // sv32 / dp32 are overwritten in place with P^T and dS^T (hi parts).
         uint32_t pl[PASSES == 3 ? 32 : 1], dl[PASSES == 3 ? 32 : 1];
@@ -403,32 +445,39 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
             dp32[t] = __float_as_uint(ds);
           }
         }
-        tmem_st32(lb + Cfg::kST + c * 32, sv32);
-        tmem_st32(lb + Cfg::kDPT + c * 32, dp32);
+        tmem_st32(lb + buf + Cfg::kST + c * 32, sv32);
+        tmem_st32(lb + buf + Cfg::kDPT + c * 32, dp32);
         if constexpr (PASSES == 3) {
-          tmem_st32(lb + Cfg::kST + NQ + c * 32, pl);
-          tmem_st32(lb + Cfg::kDPT + NQ + c * 32, dl);
+          tmem_st32(lb + buf + Cfg::kST + NQ + c * 32, pl);
+          tmem_st32(lb + buf + Cfg::kDPT + NQ + c * 32, dl);
         }
       }
-      // Observe the previous block's partial (every phase, in order); in
-      // 3xTF32 mode also add it into the masters.
+      // Observe the previous block's gradient MMAs (every phase, in order);
+      // in 3xTF32 mode fold the partial after every odd block (the next, even
+      // block's MMAs start a fresh partial once this thread arrives below).
       if (i > 0) {
-        if (PASSES == 3) {
-          if (!drain(i - 1)) {
-            ok = false;
-            break;
-          }
-        } else if (!mbar_wait_warp(&part_full, (i - 1) & 1, p.status, kStatusTimeoutAccum)) {
+        if (!mbar_wait_warp(&part_full, (i - 1) & 1, p.status, kStatusTimeoutAccum)) {
           ok = false;
           break;
+        }
+        if (PASSES == 3 && ((i - 1) & 1)) {
+          tc_fence_after();
+          fold(i - 1);
         }
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full);
+      mbar_arrive(&p_full[i & 1]);
+      if (threadIdx.x == 64) ABACUS_BWD_TRACE(2, i)
     }
-    if (ok && PASSES == 3 && nb > 0) ok = drain(nb - 1);
-    if (nb > 0 && PASSES == 1) ok = mbar_wait_warp(&part_full, (nb - 1) & 1, p.status, kStatusTimeoutAccum) && ok;
+    if (nb > 0 && ok) {
+      ok = mbar_wait_warp(&part_full, (nb - 1) & 1, p.status, kStatusTimeoutAccum);
+      if (ok && PASSES == 3) {
+        tc_fence_after();
+        fold(nb - 1);
+        tmem_st_wait();
+      }
+    }
     tc_fence_after();
     // TMEM loads are warp-collective: every lane loads, only valid rows store.
     const bool have = __all_sync(0xffffffffu, ok) && nb > 0;
@@ -489,17 +538,22 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
       fence_proxy_async_smem();
       mbar_arrive(&kv_conv);
     }
-    for (int i = 0; i < nb && ok; ++i) {
-      if (!mbar_wait_warp(&kf_full, i & 1, p.status, kStatusTimeoutFull)) break;
-      split_tile(tile(0, 0), tile(0, 1), Cfg::kQTile, ct, 128);
-      split_tile(tile(2, 0), tile(2, 1), Cfg::kQTile, ct, 128);
-      fence_proxy_async_smem();
-      mbar_arrive(&kf_conv);
-      if (!mbar_wait_warp(&mn_full, i & 1, p.status, kStatusTimeoutFull)) break;
-      split_tile(tile(1, 0), tile(1, 1), Cfg::kQTile, ct, 128);
-      split_tile(tile(3, 0), tile(3, 1), Cfg::kQTile, ct, 128);
-      fence_proxy_async_smem();
-      mbar_arrive(&mn_conv);
+    // Same order as the producer: K-major block i+1, then MN-major block i.
+    for (int step = 0; step <= nb && ok; ++step) {
+      if (step < nb) {
+        if (!mbar_wait_warp(&kf_full, step & 1, p.status, kStatusTimeoutFull)) break;
+        split_tile(tile(0, 0), tile(0, 1), Cfg::kQTile, ct, 128);
+        split_tile(tile(2, 0), tile(2, 1), Cfg::kQTile, ct, 128);
+        fence_proxy_async_smem();
+        mbar_arrive(&kf_conv);
+      }
+      if (step >= 1) {
+        if (!mbar_wait_warp(&mn_full, (step - 1) & 1, p.status, kStatusTimeoutFull)) break;
+        split_tile(tile(1, 0), tile(1, 1), Cfg::kQTile, ct, 128);
+        split_tile(tile(3, 0), tile(3, 1), Cfg::kQTile, ct, 128);
+        fence_proxy_async_smem();
+        mbar_arrive(&mn_conv);
+      }
     }
   }
 
@@ -513,6 +567,8 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
 
 // ============================================================================ dQ
 template <int D, int PASSES>
+#undef ABACUS_BWD_TRACE
+
 struct DqCfg {
   static constexpr int kOuter = 128;                    // queries per CTA
   static constexpr int kInner = (PASSES == 3 || D == 128) ? 32 : 64;  // keys per block
@@ -520,18 +576,25 @@ struct DqCfg {
   static constexpr int kQTile = kOuter * D * 4;         // Q or dO
   static constexpr int kKTile = kInner * D * 4;         // one layout of K or V
   static constexpr int kStageBytes = 3 * kKTile * kSplit;  // K_k, K_mn, V_k [+ lo]
-  static constexpr int kSmemBytes = 2 * kQTile * kSplit + kStageBytes + 1024;
+  static constexpr int kSmemRaw = 2 * kQTile * kSplit + kStageBytes + 1024;
   static constexpr int kThreads = PASSES == 3 ? 320 : 192;
   // Register cap for one CTA per SM: each of the 4 SM sub-partitions holds
   // 16384 registers and ceil(warps / 4) of the CTA's warps.
   static constexpr int kWarpsPerSubpartition = (kThreads / 32 + 3) / 4;
   static constexpr int kMaxRegs =
       (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8 > 255 ? 255 : (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8;
-  // TMEM: S, dP (dS hi [, dS lo]), dQ partials x2.
-  static constexpr int kS = 0, kDP = kInner, kDQ = kInner + kInner * kSplit;
+  // TMEM: two buffers (blocks alternate) of S and dP (dS hi [, dS lo]), so the
+  // next block's score MMAs run while the threads work on this block; then
+  // two dQ partial buffers.
+  static constexpr int kS = 0, kDP = kInner, kBufCols = kInner + kInner * kSplit;
+  static constexpr int kDQ = 2 * kBufCols;
   static constexpr int kCols = kDQ + 2 * D;
   static constexpr uint32_t kTmemCols = kCols <= 256 ? 256 : 512;
   static constexpr int kMaxBlocks = 2048;
+  // A CTA that takes all 512 TMEM columns must be alone on its SM (a second
+  // one would wait in tcgen05.alloc for the first to finish): ask for more
+  // than half of the SM's shared memory.
+  static constexpr int kSmemBytes = (kTmemCols == 512 && kSmemRaw < 116 * 1024) ? 116 * 1024 : kSmemRaw;
 };
 
 template <int D, int PASSES>
@@ -540,7 +603,7 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
   constexpr int NK = Cfg::kInner;
   static_assert(Cfg::kCols <= 512, "TMEM budget");
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t q_full, q_conv, s_full, p_full, dq_full[2], dq_empty[2];
+  __shared__ uint64_t q_full, q_conv, s_full[2], p_full[2], dq_full[2], dq_empty[2];
   // K_j / V_j tiles in two groups: K-major K and V (S, dP MMAs) and MN-major K
   // (dQ MMA), so the next block's K-major tiles load while this block's dQ runs.
   __shared__ uint64_t kf_full, kf_conv, kf_empty, mn_full, mn_conv, mn_empty;
@@ -571,8 +634,10 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
     mbar_init(&q_conv, 128);
-    mbar_init(&s_full, 1);
-    mbar_init(&p_full, 128);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(&p_full[0], 128);
+    mbar_init(&p_full[1], 128);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&dq_full[i], 1);
       mbar_init(&dq_empty[i], 128);
@@ -604,24 +669,32 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
         tma_load_2d(sq + c * 128 * 128, &p.tma_q_k, &q_full, col0 + 32 * c, q_row0);
         tma_load_2d(sdo + c * 128 * 128, &p.tma_do_k, &q_full, col0 + 32 * c, q_row0);
       }
+      // K-major K / V run one block ahead of the MN-major K: block j+1's score
+      // MMAs are issued before block j's dQ MMAs.
       int issued_k = 0, issued_mn = 0;
-      for (int j = 0; j < nb; ++j) {
-        const int krow = k_row_base + (block_list[j] & 0xFFFF) * NK;
-        if (j >= 1 && !mbar_wait(&kf_empty, (j - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&kf_full, 2 * Cfg::kKTile);
+      for (int step = 0; step <= nb; ++step) {
+        if (step < nb) {
+          const int krow = k_row_base + (block_list[step] & 0xFFFF) * NK;
+          if (step >= 1 && !mbar_wait(&kf_empty, (step - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+          mbar_arrive_expect_tx(&kf_full, 2 * Cfg::kKTile);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          tma_load_2d(tile(0, 0) + c * NK * 128, &p.tma_k_k, &kf_full, col0 + 32 * c, krow);
-          tma_load_2d(tile(2, 0) + c * NK * 128, &p.tma_v_k, &kf_full, col0 + 32 * c, krow);
+          for (int c = 0; c < D / 32; ++c) {
+            tma_load_2d(tile(0, 0) + c * NK * 128, &p.tma_k_k, &kf_full, col0 + 32 * c, krow);
+            tma_load_2d(tile(2, 0) + c * NK * 128, &p.tma_v_k, &kf_full, col0 + 32 * c, krow);
+          }
+          ++issued_k;
         }
-        ++issued_k;
-        if (j >= 1 && !mbar_wait(&mn_empty, (j - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&mn_full, Cfg::kKTile);
+        if (step >= 1) {
+          const int j = step - 1;
+          const int krow = k_row_base + (block_list[j] & 0xFFFF) * NK;
+          if (j >= 1 && !mbar_wait(&mn_empty, (j - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+          mbar_arrive_expect_tx(&mn_full, Cfg::kKTile);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          tma_load_2d(tile(1, 0) + c * NK * 128, &p.tma_k_mn, &mn_full, col0 + 32 * c, krow);
+          for (int c = 0; c < D / 32; ++c) {
+            tma_load_2d(tile(1, 0) + c * NK * 128, &p.tma_k_mn, &mn_full, col0 + 32 * c, krow);
+          }
+          ++issued_mn;
         }
-        ++issued_mn;
       }
       mbar_wait(&q_full, 0, nullptr, 0);
       if (issued_k > 0) mbar_wait(&kf_full, (issued_k - 1) & 1, nullptr, 0);
@@ -632,16 +705,17 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
       constexpr uint32_t idesc_s = idesc_tf32(128, NK, false, false);
       constexpr uint32_t idesc_dq = idesc_tf32(128, D, false, true);
       bool ok = mbar_wait(PASSES == 3 ? &q_conv : &q_full, 0, p.status, kStatusTimeoutFull);
-      for (int j = 0; j < nb && ok; ++j) {
-        if (!mbar_wait(PASSES == 3 ? &kf_conv : &kf_full, j & 1, p.status, kStatusTimeoutFull)) break;
+      // S = Q K_j^T, dP = dO V_j^T into TMEM buffer j & 1.
+      auto issue_scores = [&](int j) -> bool {
+        if (!mbar_wait(PASSES == 3 ? &kf_conv : &kf_full, j & 1, p.status, kStatusTimeoutFull)) return false;
         tc_fence_after();
-        // S = Q K^T, dP = dO V^T.
+        const int sb = (j & 1) * Cfg::kBufCols;
 #pragma unroll
         for (int pair = 0; pair < 2; ++pair) {
           const uint32_t a_hi = smem_u32(pair == 0 ? sq : sdo);
           const uint32_t b_hi = smem_u32(tile(pair == 0 ? 0 : 2, 0));
           const uint32_t b_lo = smem_u32(tile(pair == 0 ? 0 : 2, 1));
-          const uint32_t d = tmem + (pair == 0 ? Cfg::kS : Cfg::kDP);
+          const uint32_t d = tmem + sb + (pair == 0 ? Cfg::kS : Cfg::kDP);
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
 #pragma unroll
@@ -659,15 +733,18 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
             }
           }
         }
-        mma_commit(&s_full);
+        mma_commit(&s_full[j & 1]);
         mma_commit(&kf_empty);
+        return true;
+      };
+      // dQ_j = dS_j K_j into partial buffer j & 1, A from TMEM buffer j & 1.
+      auto issue_dq = [&](int j) -> bool {
         const int buf = j & 1;
-        if (!mbar_wait(&p_full, j & 1, p.status, kStatusTimeoutAccum)) break;
-        if (!mbar_wait(PASSES == 3 ? &mn_conv : &mn_full, j & 1, p.status, kStatusTimeoutFull)) break;
-        if (j >= 2 && !mbar_wait(&dq_empty[buf], ((j >> 1) - 1) & 1, p.status, kStatusTimeoutAccum)) break;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) return false;
+        if (!mbar_wait(PASSES == 3 ? &mn_conv : &mn_full, j & 1, p.status, kStatusTimeoutFull)) return false;
+        if (j >= 2 && !mbar_wait(&dq_empty[buf], ((j >> 1) - 1) & 1, p.status, kStatusTimeoutAccum)) return false;
         tc_fence_after();
-        // dQ_j = dS K_j.
-        const uint32_t a = tmem + Cfg::kDP;
+        const uint32_t a = tmem + buf * Cfg::kBufCols + Cfg::kDP;
         const uint32_t bh = smem_u32(tile(1, 0));
         const uint32_t bl = smem_u32(tile(1, 1));
         const uint32_t d = tmem + Cfg::kDQ + buf * D;
@@ -686,6 +763,14 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
         }
         mma_commit(&dq_full[buf]);
         mma_commit(&mn_empty);
+        return true;
+      };
+      if (ok && nb > 0) ok = issue_scores(0);
+      for (int j = 0; j < nb && ok; ++j) {
+        // The next block's scores go ahead of this block's dQ MMAs; their
+        // buffer was last read by block j - 1's dQ MMAs, issued earlier.
+        if (j + 1 < nb) ok = issue_scores(j + 1);
+        if (ok) ok = issue_dq(j);
       }
       if (nb > 0) {
         mbar_wait(&kf_empty, (nb - 1) & 1, p.status, kStatusTimeoutEmpty);
@@ -726,7 +811,8 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
       const int entry = block_list[j];
       const int kbk = entry & 0xFFFF;
       const bool partial = (entry >> 30) & 1;
-      if (!mbar_wait_warp(&s_full, j & 1, p.status, kStatusTimeoutAccum)) {
+      const int sb = (j & 1) * Cfg::kBufCols;
+      if (!mbar_wait_warp(&s_full[j & 1], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) {
         ok = false;
         break;
       }
@@ -734,8 +820,8 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
 #pragma unroll
       for (int c = 0; c < NK / 32; ++c) {
         uint32_t sv32[32], dp32[32];
-        tmem_ld32(lb + Cfg::kS + c * 32, sv32);
-        tmem_ld32(lb + Cfg::kDP + c * 32, dp32);
+        tmem_ld32(lb + sb + Cfg::kS + c * 32, sv32);
+        tmem_ld32(lb + sb + Cfg::kDP + c * 32, dp32);
         tmem_ld_wait();
         // dp32 is overwritten in place with dS (hi part); sv32 with dS lo.
 #pragma unroll
@@ -753,12 +839,12 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
             dp32[t] = __float_as_uint(ds);
           }
         }
-        tmem_st32(lb + Cfg::kDP + c * 32, dp32);
-        if (PASSES == 3) tmem_st32(lb + Cfg::kDP + NK + c * 32, sv32);
+        tmem_st32(lb + sb + Cfg::kDP + c * 32, dp32);
+        if (PASSES == 3) tmem_st32(lb + sb + Cfg::kDP + NK + c * 32, sv32);
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full);
+      mbar_arrive(&p_full[j & 1]);
       if (j >= 1 && !fold(j - 1)) ok = false;
     }
     if (ok && nb > 0) ok = fold(nb - 1);
@@ -778,16 +864,21 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
       fence_proxy_async_smem();
       mbar_arrive(&q_conv);
     }
-    for (int j = 0; j < nb && ok; ++j) {
-      if (!mbar_wait_warp(&kf_full, j & 1, p.status, kStatusTimeoutFull)) break;
-      split_tile(tile(0, 0), tile(0, 1), Cfg::kKTile, ct, 128);
-      split_tile(tile(2, 0), tile(2, 1), Cfg::kKTile, ct, 128);
-      fence_proxy_async_smem();
-      mbar_arrive(&kf_conv);
-      if (!mbar_wait_warp(&mn_full, j & 1, p.status, kStatusTimeoutFull)) break;
-      split_tile(tile(1, 0), tile(1, 1), Cfg::kKTile, ct, 128);
-      fence_proxy_async_smem();
-      mbar_arrive(&mn_conv);
+    // Same order as the producer: K-major block j+1, then MN-major block j.
+    for (int step = 0; step <= nb && ok; ++step) {
+      if (step < nb) {
+        if (!mbar_wait_warp(&kf_full, step & 1, p.status, kStatusTimeoutFull)) break;
+        split_tile(tile(0, 0), tile(0, 1), Cfg::kKTile, ct, 128);
+        split_tile(tile(2, 0), tile(2, 1), Cfg::kKTile, ct, 128);
+        fence_proxy_async_smem();
+        mbar_arrive(&kf_conv);
+      }
+      if (step >= 1) {
+        if (!mbar_wait_warp(&mn_full, (step - 1) & 1, p.status, kStatusTimeoutFull)) break;
+        split_tile(tile(1, 0), tile(1, 1), Cfg::kKTile, ct, 128);
+        fence_proxy_async_smem();
+        mbar_arrive(&mn_conv);
+      }
     }
   }
 

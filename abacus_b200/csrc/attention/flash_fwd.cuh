@@ -67,7 +67,7 @@ struct FwdCfg {
   static constexpr int kSplit = PASSES == 3 ? 2 : 1;
   static constexpr int kStages = 2;
   static constexpr int kStageBytes = (kKBytes + kVBytes) * kSplit;
-  static constexpr int kSmemBytes = kQBytes * kSplit + kStages * kStageBytes + 1024;
+  static constexpr int kSmemRaw = kQBytes * kSplit + kStages * kStageBytes + 1024;
   static constexpr int kThreads = PASSES == 3 ? 320 : 192;
   // Register cap for one CTA per SM: each of the 4 SM sub-partitions holds
   // 16384 registers and ceil(warps / 4) of the CTA's warps.
@@ -79,6 +79,10 @@ struct FwdCfg {
   static constexpr int kCols = kPVBase + 2 * D;
   static constexpr uint32_t kTmemCols = kCols <= 256 ? 256 : 512;
   static constexpr int kMaxBlocks = 2048;  // key blocks per sequence (Lk <= 131072)
+  // A CTA that takes all 512 TMEM columns must be alone on its SM (a second
+  // one would wait in tcgen05.alloc for the first to finish): ask for more
+  // than half of the SM's shared memory.
+  static constexpr int kSmemBytes = (kTmemCols == 512 && kSmemRaw < 116 * 1024) ? 116 * 1024 : kSmemRaw;
 };
 
 

@@ -35,6 +35,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_push_rows", &abacus::comm::tp_push_rows, "SP shard -> every rank's gathered buffer + epoch flags");
   m.def("tp_reduce_rows", &abacus::comm::tp_reduce_rows, "sum of scattered partial slots (+ residual) after arrival");
   m.def("ep_push_rows", &abacus::comm::ep_push_rows, "expert-parallel dispatch: rows into their experts' slabs on peers");
+  m.def("ep_credit", &abacus::comm::ep_credit, "credit rows that will never return to an expert-parallel counter");
   m.def("ep_combine", &abacus::comm::ep_combine, "expert-parallel combine: weighted sum of returned rows");
   m.def("ar_adamw", &abacus::comm::ar_adamw, "peer-memory gradient reduce + AdamW + parameter broadcast");
   m.def("read_status", &abacus::host::read_status, "device status word (0 = healthy)");

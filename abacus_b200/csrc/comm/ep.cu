@@ -17,6 +17,12 @@
 // * ep_combine (source side): waits until every row came back, then
 //   out[t] = sum_j w[t, j] * ret[t*k + j] in slot order (or the plain sum).
 //
+// With a capacity (static slabs: every source owns a fixed-size region of
+// each expert's slab, so no counts exchange and no host sync is needed), an
+// assignment over its expert's capacity has dest_rank -1 and is not sent;
+// its source credits the missing rows to its own return counter (ep_credit)
+// and gives the slot weight 0 in the combine.
+//
 // All waits are bounded (ABACUS_PEER_WAIT_NS) and record kStatusTimeoutPeer.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -50,6 +56,7 @@ __global__ void __launch_bounds__(256) ep_push_kernel(const __grid_constant__ Ep
     for (long long a = static_cast<long long>(blockIdx.x) * warps + warp; a < assignments;
          a += static_cast<long long>(gridDim.x) * warps) {
       const int r = dest_rank[a];
+      if (r < 0) continue;  // dropped (over its expert's capacity): not sent
       const long long row = dest_row[a];
       const float s = scale ? scale[a] : 1.f;
       const float4* in = reinterpret_cast<const float4*>(src + (a / top_k) * dim);
@@ -97,6 +104,9 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < top_k; ++j) {
       const float w = weights ? weights[t * top_k + j] : 1.f;
+      // A zero weight marks a slot with nothing to add (an assignment dropped
+      // over capacity has no returned row; its buffer row is stale).
+      if (w == 0.f) continue;
       const float4 v = reinterpret_cast<const float4*>(ret + (t * top_k + j) * dim)[c];
       acc.x += w * v.x;
       acc.y += w * v.y;
@@ -107,7 +117,28 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict
   }
 }
 
+// Adds amount[0] * multiplier to a return counter on this GPU. Rows that were
+// never sent (dropped over capacity) never come back; crediting them keeps the
+// counter target a host-side constant. Atomic against the peers' concurrent
+// system-scope adds to the same counter.
+__global__ void ep_credit_kernel(int* counter, const int* amount, int multiplier) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    const int add = amount[0] * multiplier;
+    if (add != 0) atomicAdd(counter, add);
+  }
+}
+
 }  // namespace
+
+void ep_credit(torch::Tensor counter, torch::Tensor amount, int64_t multiplier) {
+  const c10::cuda::CUDAGuard guard(counter.device());
+  TORCH_CHECK(counter.is_cuda() && counter.scalar_type() == torch::kInt32 && counter.numel() >= 1, "counter");
+  TORCH_CHECK(amount.is_cuda() && amount.scalar_type() == torch::kInt32 && amount.numel() >= 1, "amount: int32");
+  ep_credit_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(counter.data_ptr<int>(), amount.data_ptr<int>(),
+                                                                    static_cast<int>(multiplier));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  host::note_launch();
+}
 
 void ep_push_rows(torch::Tensor src, int64_t top_k, torch::Tensor dest_rank, torch::Tensor dest_row,
                   c10::optional<torch::Tensor> scale, std::vector<int64_t> row_ptrs, std::vector<int64_t> meta_ptrs,

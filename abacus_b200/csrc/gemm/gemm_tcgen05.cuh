@@ -93,8 +93,9 @@ struct alignas(64) Params {
   unsigned* scatter_counter[8];
   int scatter_chunk, scatter_seq;
   // Row-map scatter (expert parallel combine): with scatter_meta set, output
-  // row r goes to rank meta[r] & 7 at row meta[r] >> 3, and each tile adds to
-  // every destination's counter the number of its rows that went there.
+  // row r goes to rank meta[r] & 7 at row meta[r] >> 3 (not at all when
+  // meta[r] < 0), and each tile adds to every destination's counter the
+  // number of its rows that went there.
   const int* scatter_meta;
   int* status;
 };
@@ -485,7 +486,9 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
           float v[32];
           group(c, v);
           const int col0 = n0 + c * 32;
-          if (row_ok && col0 < p.N) {
+          // Row-map scatter: rows whose meta is negative (unfilled capacity
+          // slots of an expert slab) are computed but not returned.
+          if (row_ok && col0 < p.N && (!p.scatter_meta || p.scatter_meta[row] >= 0)) {
             float* crow;
             if (p.scatter_meta) {
               const int meta = p.scatter_meta[row];
@@ -634,7 +637,8 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
         __threadfence_system();
         if (lane == 0) epi_ok[q] = ok ? 1 : 0;
         named_barrier_sync(1, 128);
-        const int dest = row_ok ? (p.scatter_meta[row] & 7) : -1;
+        const int meta_row = row_ok ? p.scatter_meta[row] : -1;
+        const int dest = meta_row >= 0 ? (meta_row & 7) : -1;
   #pragma unroll
         for (int d = 0; d < 8; ++d) {
           const unsigned n = __popc(__ballot_sync(0xffffffffu, dest == d));

@@ -175,6 +175,29 @@ def _grouped_experts(x_TD, weights_TK, indices_TK, w_gate_EDM, w_up_EDM, w_down_
     return x_TD.new_zeros(x_TD.shape).index_add(0, token_of, y)
 
 
+def _grouped_experts_capacity(x_TD, weights_TK, indices_TK, w_gate_EDM, w_up_EDM, w_down_EMD, capacity):
+    """``_grouped_experts`` with static capacity slabs: expert e's rows are
+    slots [e*C, (e+1)*C) of one (E*C, D) slab, filled in (token, slot) order;
+    assignments past an expert's capacity go to a discarded extra row (the
+    router has already given them weight 0). Every expert GEMM has C rows, so
+    nothing about the routing reaches the host."""
+    t, k = indices_TK.shape
+    n_experts = w_gate_EDM.shape[0]
+    flat_e = indices_TK.reshape(-1)
+    onehot = torch.nn.functional.one_hot(flat_e, n_experts)
+    within = (onehot.cumsum(dim=0) * onehot).sum(dim=-1) - 1
+    keep = within < capacity
+    spill = n_experts * capacity
+    slot = torch.where(keep, flat_e * capacity + within, spill)
+    token_of = torch.arange(t, device=x_TD.device).repeat_interleave(k)
+    slab = x_TD.new_zeros(spill + 1, x_TD.shape[1]).index_copy(0, slot, x_TD.index_select(0, token_of))
+    outs = [_expert_forward(slab[e * capacity : (e + 1) * capacity], w_gate_EDM[e], w_up_EDM[e], w_down_EMD[e])
+            for e in range(n_experts)]
+    y_slab = torch.cat(outs + [x_TD.new_zeros(1, x_TD.shape[1])], dim=0)
+    y_TKD = y_slab.index_select(0, slot).view(t, k, -1)
+    return (y_TKD * (weights_TK * keep.view(t, k)).unsqueeze(-1)).sum(dim=1)
+
+
 class MoE(torch.nn.Module):
     """Top-k mixture of SwiGLU experts (single process)."""
 
@@ -218,8 +241,8 @@ class MoE(torch.nn.Module):
         tokens = x_BLD.shape[0] * x_BLD.shape[1]
         weights_TK = weights_BLK.reshape(tokens, self.top_k)
         indices_TK = indices_BLK.reshape(tokens, self.top_k)
-        if self.capacity_factor is not None and tokens > 0:
-            capacity = math.ceil(self.capacity_factor * tokens * self.top_k / self.n_experts)
+        capacity = self._capacity(tokens)
+        if capacity is not None:
             weights_TK = weights_TK * _capacity_keep(indices_TK, self.n_experts, capacity)
         return weights_TK, indices_TK
 
@@ -229,8 +252,19 @@ class MoE(torch.nn.Module):
         x_TD = x_BLD.reshape(batch * length, self.dim)
         if x_TD.shape[0] == 0:
             return x_BLD
-        out_TD = _grouped_experts(x_TD, weights_TK, indices_TK, self.w_gate_EDM, self.w_up_EDM, self.w_down_EMD)
+        capacity = self._capacity(x_TD.shape[0])
+        if capacity is not None and x_TD.is_cuda:
+            out_TD = _grouped_experts_capacity(x_TD, weights_TK, indices_TK, self.w_gate_EDM, self.w_up_EDM,
+                                               self.w_down_EMD, capacity)
+        else:
+            out_TD = _grouped_experts(x_TD, weights_TK, indices_TK, self.w_gate_EDM, self.w_up_EDM, self.w_down_EMD)
         return out_TD.reshape(batch, length, self.dim)
+
+    def _capacity(self, tokens: int) -> int | None:
+        """Per-expert capacity of this rank's tokens (None without a capacity factor)."""
+        if self.capacity_factor is None or tokens == 0:
+            return None
+        return math.ceil(self.capacity_factor * tokens * self.top_k / self.n_experts)
 
 
 class MoEExpertParallel(torch.nn.Module):
@@ -288,6 +322,7 @@ class MoEExpertParallel(torch.nn.Module):
         self._ep_key = tp_fused.new_key("moe")
 
     _route = MoE._route
+    _capacity = MoE._capacity
 
     def forward(self, x_BLD: torch.Tensor) -> torch.Tensor:
         if self.world_size == 1:
@@ -318,7 +353,14 @@ class MoEExpertParallel(torch.nn.Module):
         local experts, send results back, weight and sum the K slots."""
         if ep_fused.usable(local_SD, self.hidden_dim):
             # Dispatch fused with the permutation, combine fused into the
-            # expert down-projection's epilogue (NVLink peer memory).
+            # expert down-projection's epilogue (NVLink peer memory). With a
+            # capacity and every routed token local (EP over DP ranks), the
+            # slabs are static and the routing never reaches the host.
+            capacity = self._capacity(local_SD.shape[0]) if self.data_parallel else None
+            if capacity is not None:
+                return ep_fused.dispatch_combine_capacity(local_SD, weights_SK, indices_SK, self.w_gate_EDM,
+                                                          self.w_up_EDM, self.w_down_EMD, self.n_experts, capacity,
+                                                          self._ep_key)
             return ep_fused.dispatch_combine(local_SD, weights_SK, indices_SK, self.w_gate_EDM, self.w_up_EDM,
                                              self.w_down_EMD, self.n_experts, self._ep_key)
         n_local = local_SD.shape[0]

@@ -24,6 +24,17 @@ Backward mirrors it: the weighted output gradient is pushed to the experts'
 slabs, the SwiGLU backward GEMM waits for it, and the dX GEMM's epilogue
 returns each row to its source, which sums the slots. Router-weight gradients
 are <dY_t, y_slot> from the returned rows.
+
+With a capacity factor (``dispatch_combine_capacity``) the slabs are static
+and nothing leaves the device: each expert's slab on its owner holds
+``world * C`` rows, source rank r owning rows [r*C, (r+1)*C), where C is the
+per-rank capacity of the router (the first C assignments of each expert in
+(token, slot) order are kept, the rest dropped, exactly the router's capacity
+rule). A row's destination is then a function of its own rank's routing only,
+so there is no counts exchange and no host sync; the expert GEMMs have fixed
+shapes. Unfilled slab rows carry a negative meta (their outputs are not
+returned) and zero gradients; dropped assignments are credited to the return
+counter by their source and get weight 0 in the combine.
 """
 from __future__ import annotations
 
@@ -196,6 +207,147 @@ class _EPFused(torch.autograd.Function):
         # Router weights: d w[t, j] = <dY_t, y_(t, j)>, from the rows returned in forward.
         d_weights = (ret_rows.view(n, top_k, dim) * grad_out.unsqueeze(1)).sum(dim=-1)
         return dx, d_weights, None, d_gate, d_up, d_down, None, None
+
+
+def _static_plan(indices, n_experts, local_experts, capacity, ws):
+    """Device-side placement of every assignment into the static slabs:
+    (dest_rank, dest_row) int32 (dest_rank -1 = dropped), the keep mask and
+    the number of dropped assignments (int32, on the device)."""
+    flat_e = indices.reshape(-1)
+    onehot = torch.nn.functional.one_hot(flat_e, n_experts)
+    within = (onehot.cumsum(dim=0) * onehot).sum(dim=-1) - 1  # rank among this expert's assignments
+    keep = within < capacity
+    slab = ws.world * capacity
+    dest_rank = torch.where(keep, torch.div(flat_e, local_experts, rounding_mode="floor"), -1).to(torch.int32)
+    dest_row = ((flat_e % local_experts) * slab + ws.rank * capacity + within.clamp(max=capacity - 1)).to(torch.int32)
+    dropped = (~keep).sum().to(torch.int32).reshape(1)
+    return dest_rank.contiguous(), dest_row.contiguous(), keep, dropped
+
+
+def _static_slab(ws, key, rows, dim):
+    """Static receive slab `key` (rows x dim, zeroed) and its meta (all -1) on
+    every rank, created once."""
+    fresh = key not in ws._buffers
+    buf, ptrs = ws.buffer(key, rows * dim)
+    meta_buf, meta_ptrs = ws.buffer(key + ".meta", rows)
+    if fresh:
+        buf.zero_()
+        meta_buf.view(torch.int32).fill_(-1)
+        torch.cuda.synchronize(buf.device)
+        dist.barrier(group=ws.group)  # every slab is clean before any peer pushes into it
+    return buf[: rows * dim].view(rows, dim), ptrs, meta_buf[:rows].view(torch.int32), meta_ptrs
+
+
+def _static_push(ws, key, src, top_k, dest_rank, dest_row, scale, rows, dim):
+    slab, ptrs, meta, meta_ptrs = _static_slab(ws, key, rows, dim)
+    off = ws.slots(key)
+    epoch = ws.next_epoch(key)
+    done = ws._done.get(key)
+    if done is None:
+        done = ws._done[key] = torch.zeros(1, dtype=torch.int32, device=src.device)
+    flags = [p + 4 * (off + ws.rank) for p in ws.signal_ptrs]
+    ext().ep_push_rows(src, top_k, dest_rank, dest_row, scale, ptrs, meta_ptrs, flags, ws.rank, epoch, done)
+    wait = [ws.signal_ptrs[ws.rank] + 4 * off, 2, epoch, 1, ws.world, ws.rank]
+    return slab, meta, wait
+
+
+class _EPFusedCapacity(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weights, indices, w_gate, w_up, w_down, n_experts, capacity, key):
+        ws = tp_fused.workspace(x.device, DIM)
+        ws.begin_step()
+        call = ws.call_key(key)
+        n, dim = x.shape
+        top_k = indices.shape[1]
+        local_experts = w_gate.shape[0]
+        hidden = w_gate.shape[2]
+        passes = precision.passes()
+        slab_rows = ws.world * capacity
+        rows = local_experts * slab_rows
+        dest_rank, dest_row, keep, dropped = _static_plan(indices, n_experts, local_experts, capacity, ws)
+        xs_all, meta, wait = _static_push(ws, call + ".X", x.contiguous(), top_k, dest_rank, dest_row, None, rows, dim)
+        ret, ret_ptrs, counter_ptrs, counter = _return_target(ws, call + ".R", n * top_k, dim)
+        n_tiles = ext().gemm_n_tiles(dim, passes)
+        saved = []
+        for le in range(local_experts):
+            xs = xs_all[le * slab_rows : (le + 1) * slab_rows]
+            g = torch.empty(slab_rows, hidden, device=x.device, dtype=torch.float32)
+            u = torch.empty_like(g)
+            h = torch.empty_like(g)
+            ext().gemm_swiglu_tp(xs, w_gate[le], w_up[le], g, u, h, passes, wait)
+            mrow = meta[le * slab_rows : (le + 1) * slab_rows]
+            scatter = [-1, mrow.data_ptr()] + list(ret_ptrs) + list(counter_ptrs)
+            ext().gemm_out_tp(ret[:dim].view(1, dim), h, [w_down[le]], False, False, _SINGLE, 1.0, passes, None,
+                              scatter)
+            saved.append((g, u, h))
+        ext().ep_credit(counter, dropped, n_tiles)
+        target = ws.add_target(call + ".R", n * top_k * n_tiles)
+        out = torch.empty(n, dim, device=x.device, dtype=torch.float32)
+        ret_rows = ret[: n * top_k * dim].view(n * top_k, dim)
+        w_kept = (weights.reshape(-1) * keep).contiguous()
+        ext().ep_combine(ret_rows, w_kept, top_k, counter, target, out)
+        ctx.save_for_backward(weights, w_gate, w_up, w_down, keep, dest_rank, dest_row, dropped)
+        ctx.saved = saved
+        ctx.meta = (call, n, dim, top_k, hidden, capacity, local_experts)
+        ctx.buffers = (xs_all, meta, ret_rows)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        weights, w_gate, w_up, w_down, keep, dest_rank, dest_row, dropped = ctx.saved_tensors
+        call, n, dim, top_k, hidden, capacity, local_experts = ctx.meta
+        xs_all, meta, ret_rows = ctx.buffers
+        ws = tp_fused.workspace(grad_out.device, DIM)
+        ws._backward_seen = True
+        passes = precision.passes()
+        grad_out = grad_out.contiguous()
+        slab_rows = ws.world * capacity
+        rows = local_experts * slab_rows
+        scale = weights.reshape(-1).contiguous()
+        dy_all, dy_meta, wait = _static_push(ws, call + ".dY", grad_out, top_k, dest_rank, dest_row, scale, rows, dim)
+        dret, dret_ptrs, counter_ptrs, counter = _return_target(ws, call + ".dR", n * top_k, dim)
+        d_gate = torch.empty_like(w_gate)
+        d_up = torch.empty_like(w_up)
+        d_down = torch.empty_like(w_down)
+        for le, (g, u, h) in enumerate(ctx.saved):
+            lo, hi = le * slab_rows, (le + 1) * slab_rows
+            dys = dy_all[lo:hi]
+            dgu = torch.empty(slab_rows, 2 * hidden, device=grad_out.device, dtype=torch.float32)
+            ext().gemm_swiglu_bwd_tp(dys, w_down[le], g, u, dgu, passes, wait)
+            scatter = [-1, meta[lo:hi].data_ptr()] + list(dret_ptrs) + list(counter_ptrs)
+            ext().gemm_out_tp(dret[:dim].view(1, dim), dgu, [w_gate[le], w_up[le]], False, True, _SEG_K, 1.0,
+                              passes, None, scatter)
+            xs = xs_all[lo:hi]
+            # Unfilled slab rows hold zero gradients (their dY rows are zero),
+            # so they add nothing to the weight gradients.
+            ext().gemm_out(d_gate[le], xs, [dgu[:, :hidden]], True, False, _SINGLE, 1.0, None, False, passes)
+            ext().gemm_out(d_up[le], xs, [dgu[:, hidden:]], True, False, _SINGLE, 1.0, None, False, passes)
+            ext().gemm_out(d_down[le], h, [dys], True, False, _SINGLE, 1.0, None, False, passes)
+        dx_tiles = ext().gemm_n_tiles(dim, passes)
+        ext().ep_credit(counter, dropped, dx_tiles)
+        target = ws.add_target(call + ".dR", n * top_k * dx_tiles)
+        dx = torch.empty(n, dim, device=grad_out.device, dtype=torch.float32)
+        ext().ep_combine(dret[: n * top_k * dim].view(n * top_k, dim), keep.to(torch.float32).contiguous(), top_k,
+                         counter, target, dx)
+        # This rank's slabs are read for the last time above: clear the meta
+        # and the gradient rows its peers filled, before this rank reaches the
+        # next step's barrier (after which peers push again).
+        meta.fill_(-1)
+        dy_all.zero_()
+        # Router weights: d w[t, j] = <dY_t, y_(t, j)> for kept slots, 0 for dropped ones.
+        d_weights = torch.where(keep.view(n, top_k),
+                                (ret_rows.view(n, top_k, dim) * grad_out.unsqueeze(1)).sum(dim=-1),
+                                torch.zeros((), device=grad_out.device))
+        return dx, d_weights, None, d_gate, d_up, d_down, None, None, None
+
+
+def dispatch_combine_capacity(x_SD, weights_SK, indices_SK, w_gate_EDM, w_up_EDM, w_down_EMD, n_experts, capacity,
+                              key):
+    """``dispatch_combine`` with static capacity-bounded slabs (no host sync):
+    assignments beyond the first ``capacity`` of their expert on this rank
+    (in (token, slot) order) are dropped."""
+    return _EPFusedCapacity.apply(x_SD.contiguous(), weights_SK, indices_SK, w_gate_EDM, w_up_EDM, w_down_EMD,
+                                  n_experts, int(capacity), key)
 
 
 def dispatch_combine(x_SD, weights_SK, indices_SK, w_gate_EDM, w_up_EDM, w_down_EMD, n_experts, key):

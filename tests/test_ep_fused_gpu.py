@@ -13,11 +13,11 @@ from _dist import run_ranks
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
-def _layer(device):
+def _layer(device, capacity_factor):
     from abacus_b200.models.moe import MoEExpertParallel
 
     torch.manual_seed(0)
-    return MoEExpertParallel(256, 4, 2, hidden_dim=512, router="softmax", capacity_factor=1.25,
+    return MoEExpertParallel(256, 4, 2, hidden_dim=512, router="softmax", capacity_factor=capacity_factor,
                              data_parallel=True).to(device)
 
 
@@ -33,28 +33,30 @@ def _check(rank, world):
 
     device = torch.device("cuda", rank)
     mesh.init_mesh(dp=world, ep=world)
-    fused_layer, plain_layer = _layer(device), _layer(device)
-    torch.manual_seed(10 + rank)  # each rank routes its own tokens
-    x = torch.randn(2, 96, 256, device=device)
-    results = []
-    for flag, layer in (("1", fused_layer), ("0", plain_layer)):
-        os.environ["ABACUS_EP_FUSED"] = flag
-        xi = x.clone().requires_grad_()
-        for _ in range(2):  # second call reuses the buffers after a backward
-            layer.zero_grad()
-            xi.grad = None
-            out = layer(xi)
-            (out * torch.linspace(-1, 1, out.numel(), device=device).view_as(out)).sum().backward()
-        results.append((out.detach(), xi.grad.clone(), [p.grad.clone() for p in layer.parameters()]))
-    os.environ["ABACUS_EP_FUSED"] = "1"
-    torch.cuda.synchronize()
-    check_status()
-    (of, xf, gf), (op, xp, gp) = results
-    assert _rel(of, op) < 1e-5
-    assert _rel(xf, xp) < 2e-4
-    for (name, _), a, b in zip(fused_layer.named_parameters(), gf, gp):
-        assert _rel(a, b) < 2e-4, name
-    assert tp_fused._WORKSPACES, "the fused path did not run"
+    # capacity 1.25: static capacity slabs (no host sync); None: counts exchange.
+    for capacity_factor in (1.25, None):
+        fused_layer, plain_layer = _layer(device, capacity_factor), _layer(device, capacity_factor)
+        torch.manual_seed(10 + rank)  # each rank routes its own tokens
+        x = torch.randn(2, 96, 256, device=device)
+        results = []
+        for flag, layer in (("1", fused_layer), ("0", plain_layer)):
+            os.environ["ABACUS_EP_FUSED"] = flag
+            xi = x.clone().requires_grad_()
+            for _ in range(3):  # later calls reuse the buffers after a backward
+                layer.zero_grad()
+                xi.grad = None
+                out = layer(xi)
+                (out * torch.linspace(-1, 1, out.numel(), device=device).view_as(out)).sum().backward()
+            results.append((out.detach(), xi.grad.clone(), [p.grad.clone() for p in layer.parameters()]))
+        os.environ["ABACUS_EP_FUSED"] = "1"
+        torch.cuda.synchronize()
+        check_status()
+        (of, xf, gf), (op, xp, gp) = results
+        assert _rel(of, op) < 1e-5, capacity_factor
+        assert _rel(xf, xp) < 2e-4, capacity_factor
+        for (name, _), a, b in zip(fused_layer.named_parameters(), gf, gp):
+            assert _rel(a, b) < 2e-4, (name, capacity_factor)
+        assert tp_fused._WORKSPACES, "the fused path did not run"
 
     # Trainer steps of a small EP + DP MoE model on both paths.
     from abacus_b200.distributed.data_parallel import DataParallel

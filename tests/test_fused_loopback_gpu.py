@@ -1,0 +1,192 @@
+"""Fused compute + collective kernels in loopback on ONE GPU.
+
+The tensor-parallel, context-parallel and data-parallel kernels take tables of
+peer pointers. Here P emulated ranks live on one GPU: every "peer" buffer is
+a separate allocation on cuda:0, and the ranks' kernels are launched one after
+another on one stream in dependency order (all pushes before any consumer), so
+no kernel ever waits for a kernel that has not already finished: every flag a
+consumer waits on is set before it starts. The results are compared with a
+PyTorch fp64 / fp32 oracle of the collective followed by the computation
+(the multi-GPU tests compare the same kernels across real NVLink peers).
+
+Covered: the sequence-parallel all-gather fused into a waiting GEMM
+(``tp_push_rows`` + ``gemm_out_tp`` wait), the GEMM -> reduce-scatter
+epilogue with the owner-side reduction (``gemm_out_tp`` scatter +
+``tp_reduce_rows``), the context-parallel flash forward over pushed K / V
+(``flash_attn_fwd_cp``), and the data-parallel reduce + AdamW + broadcast
+(``ar_adamw``).
+"""
+import math
+
+import pytest
+import torch
+
+from abacus_b200.ops import precision
+from abacus_b200.ops._ext import check_status, ext
+
+pytestmark = pytest.mark.gpu
+
+SINGLE = 0
+WORLD = 2
+
+
+def _rel(a, b):
+    return ((a.double() - b.double()).abs().max() / b.double().abs().max().clamp(min=1e-30)).item()
+
+
+def _signals(n=256):
+    return [torch.zeros(n, dtype=torch.int32, device="cuda") for _ in range(WORLD)]
+
+
+def _ptr(t, offset_elems=0):
+    return t.data_ptr() + offset_elems * t.element_size()
+
+
+def _push_all(shards, gathered, sig, off, chunk, seq, epoch):
+    """Every emulated rank pushes its shard into every rank's gathered buffer."""
+    for r, x in enumerate(shards):
+        done = torch.zeros(1, dtype=torch.int32, device="cuda")
+        flags = [_ptr(sig[p], off + r) for p in range(WORLD)]
+        ext().tp_push_rows(x, [g.data_ptr() for g in gathered], flags, chunk, seq, r, epoch, done)
+
+
+def _gathered_reference(shards, batch, chunk):
+    """(B*L, D): rank r's rows sit at b*L + r*chunk + i."""
+    parts = [x.view(batch, chunk, -1) for x in shards]
+    return torch.cat(parts, dim=1).reshape(batch * chunk * len(shards), -1)
+
+
+@pytest.mark.parametrize("passes", [3, 1])
+def test_sequence_parallel_gather_into_waiting_gemm(passes):
+    torch.manual_seed(0)
+    batch, chunk, dim, n = 2, 128, 256, 384
+    seq = chunk * WORLD
+    shards = [torch.randn(batch * chunk, dim, device="cuda") for _ in range(WORLD)]
+    w = torch.randn(dim, n, device="cuda") / math.sqrt(dim)
+    gathered = [torch.full((batch * seq, dim), float("nan"), device="cuda") for _ in range(WORLD)]
+    sig = _signals()
+    off, epoch = 16, 1
+    _push_all(shards, gathered, sig, off, chunk, seq, epoch)
+    want = _gathered_reference(shards, batch, chunk)
+    for r in range(WORLD):
+        out = torch.empty(batch * seq, n, device="cuda")
+        wait = [_ptr(sig[r], off), 0, epoch, chunk, seq, r]
+        ext().gemm_out_tp(out, gathered[r], [w], False, False, SINGLE, 1.0, passes, wait, None)
+        torch.cuda.synchronize()
+        check_status()
+        assert torch.equal(gathered[r], want)
+        tol = 1e-5 if passes == 3 else 5e-3
+        assert _rel(out, want.double() @ w.double()) < tol
+
+
+@pytest.mark.parametrize("passes", [3, 1])
+def test_gemm_reduce_scatter_epilogue_and_owner_reduction(passes):
+    torch.manual_seed(1)
+    batch, chunk, k, n = 2, 128, 192, 256
+    seq = chunk * WORLD
+    rows_local = batch * chunk
+    # Row-parallel: every rank holds a partial (B*L, k) input and its own W slice.
+    a = [torch.randn(batch * seq, k, device="cuda") for _ in range(WORLD)]
+    w = [torch.randn(k, n, device="cuda") / math.sqrt(k) for _ in range(WORLD)]
+    residual = [torch.randn(rows_local, n, device="cuda") for _ in range(WORLD)]
+    slot = rows_local * n
+    staging = [torch.full((WORLD, rows_local, n), float("nan"), device="cuda") for _ in range(WORLD)]
+    sig = _signals()
+    off = 32
+    target = None
+    for r in range(WORLD):
+        scatter = [chunk, seq]
+        scatter += [_ptr(staging[p], r * slot) for p in range(WORLD)]
+        scatter += [_ptr(sig[p], off + r) for p in range(WORLD)]
+        tiles = ext().gemm_out_tp(staging[r][r], a[r], [w[r]], False, False, SINGLE, 1.0, passes, None, scatter)
+        target = int(tiles)
+    full = sum(a[r].double() @ w[r].double() for r in range(WORLD)).view(batch, WORLD, chunk, n)
+    for p in range(WORLD):
+        out = torch.empty(rows_local, n, device="cuda")
+        ext().tp_reduce_rows(staging[p], WORLD, sig[p][off : off + WORLD], target, residual[p], out)
+        torch.cuda.synchronize()
+        check_status()
+        want = full[:, p].reshape(rows_local, n) + residual[p].double()
+        tol = 1e-5 if passes == 3 else 5e-3
+        assert _rel(out, want) < tol
+
+
+def _attention_reference(q, k, v, q_pos, k_pos, batch, heads, hd):
+    qh = q.double().view(batch, -1, heads, hd).transpose(1, 2)
+    kh = k.double().view(batch, -1, heads, hd).transpose(1, 2)
+    vh = v.double().view(batch, -1, heads, hd).transpose(1, 2)
+    s = qh @ kh.transpose(-1, -2) / math.sqrt(hd)
+    mask = k_pos.view(1, -1) > q_pos.view(-1, 1)
+    s = s.masked_fill(mask, float("-inf"))
+    return (torch.softmax(s, dim=-1) @ vh).transpose(1, 2).reshape(q.shape[0], heads * hd)
+
+
+def _zigzag(rank, world, seq_len):
+    chunk = seq_len // (2 * world)
+    first = torch.arange(rank * chunk, (rank + 1) * chunk)
+    second = torch.arange((2 * world - 1 - rank) * chunk, (2 * world - rank) * chunk)
+    return torch.cat((first, second))
+
+
+def test_context_parallel_flash_forward_over_pushed_kv():
+    """Each rank holds a zigzag pair of chunks; K / V of every rank are pushed
+    into every rank's gathered buffer and the flash kernel waits for the
+    owners' epochs before reading them."""
+    precision.set_precision("fp32")
+    torch.manual_seed(2)
+    batch, heads, hd = 2, 4, 64
+    seq_len = 512
+    local = seq_len // WORLD  # two chunks of 128 per rank
+    hk = heads * hd
+    qs, kvs, poss = [], [], []
+    for r in range(WORLD):
+        pos = _zigzag(r, WORLD, seq_len).cuda()
+        poss.append(pos)
+        qs.append(torch.randn(batch * local, hk, device="cuda"))
+        kvs.append(torch.randn(batch * local, 2 * hk, device="cuda"))
+    gathered = [torch.full((batch * seq_len, 2 * hk), float("nan"), device="cuda") for _ in range(WORLD)]
+    sig = _signals()
+    off, epoch = 64, 1
+    _push_all(kvs, gathered, sig, off, local, seq_len, epoch)
+    k_pos = torch.cat(poss).to(torch.int64)
+    all_kv = _gathered_reference(kvs, batch, local)
+    for r in range(WORLD):
+        out = torch.empty(batch * local, hk, device="cuda")
+        lse = torch.empty(batch, heads, local, device="cuda")
+        ext().flash_attn_fwd_cp(qs[r], gathered[r][:, :hk], gathered[r][:, hk:], out, lse, batch, heads, hd, local,
+                                seq_len, 1.0 / math.sqrt(hd), poss[r].to(torch.int64), k_pos, 3,
+                                [_ptr(sig[r], off), epoch, WORLD, r])
+        torch.cuda.synchronize()
+        check_status()
+        want = _attention_reference(qs[r], all_kv[:, :hk], all_kv[:, hk:], poss[r], k_pos, batch, heads, hd)
+        assert _rel(out, want) < 1e-5
+
+
+def test_data_parallel_reduce_adamw_broadcast():
+    """Rank r reduces its slice of both ranks' gradients (token-weighted),
+    applies AdamW and stores the result into both replicas."""
+    torch.manual_seed(3)
+    n = 4096 * 3
+    grads = [torch.randn(n, device="cuda") for _ in range(WORLD)]
+    w0 = torch.randn(n, device="cuda")
+    params = [w0.clone() for _ in range(WORLD)]
+    counts = torch.tensor([300.0, 100.0], device="cuda")
+    half = n // WORLD
+    moments = [(torch.zeros(half, device="cuda"), torch.zeros(half, device="cuda")) for _ in range(WORLD)]
+    lr, b1, b2, eps, wd = 1e-3, 0.9, 0.95, 1e-8, 0.1
+    for step in (1, 2):
+        for r in range(WORLD):
+            ext().ar_adamw([g.data_ptr() for g in grads], [p.data_ptr() for p in params], counts, True, r,
+                           r * half, (r + 1) * half, moments[r][0], moments[r][1], lr, b1, b2, eps, wd, step, 0)
+    torch.cuda.synchronize()
+    check_status()
+    # Oracle: two AdamW steps on the token-weighted mean gradient.
+    g = (grads[0].double() * 300 + grads[1].double() * 100) / 400
+    w, m, v = w0.double(), torch.zeros_like(g), torch.zeros_like(g)
+    for step in (1, 2):
+        w = w * (1 - lr * wd)
+        m = m + (1 - b1) * (g - m)
+        v = b2 * v + (1 - b2) * g * g
+        w = w - lr / (1 - b1**step) * m / ((v / (1 - b2**step)).sqrt() + eps)
+    assert torch.equal(params[0], params[1])
+    assert _rel(params[0], w) < 1e-6

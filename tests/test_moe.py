@@ -102,3 +102,28 @@ def test_load_balancing_loss_values():
     assert load_balancing_loss(torch.zeros(0, 3), torch.zeros(0, dtype=torch.long)).item() == 0.0
     with pytest.raises(ValueError):
         load_balancing_loss(probs, torch.zeros(4, 1, 1, dtype=torch.long))
+
+
+def test_capacity_slabs_match_dynamic_grouping():
+    """Static capacity slabs (no host sync) give the dynamic grouping's result
+    with the router's capacity mask applied, values and gradients."""
+    from abacus_b200.models.moe import _capacity_keep, _grouped_experts, _grouped_experts_capacity
+
+    torch.manual_seed(0)
+    t, k, e, d, m = 40, 2, 4, 8, 12
+    x = torch.randn(t, d, requires_grad=True)
+    idx = torch.randint(0, e, (t, k))
+    idx[:, 1] = (idx[:, 0] + 1) % e  # distinct experts per token
+    w = torch.rand(t, k, requires_grad=True)
+    gate, up, down = (torch.randn(e, d, m) * 0.3).requires_grad_(), (torch.randn(e, d, m) * 0.3).requires_grad_(), \
+        (torch.randn(e, m, d) * 0.3).requires_grad_()
+    capacity = 15  # < t*k/e = 20 on average: some assignments drop
+    keep = _capacity_keep(idx, e, capacity)
+    assert not keep.all()
+    want = _grouped_experts(x, w * keep, idx, gate, up, down)
+    got = _grouped_experts_capacity(x, w * keep, idx, gate, up, down, capacity)
+    torch.testing.assert_close(got, want, rtol=1e-5, atol=1e-6)
+    gw = torch.autograd.grad(want.square().sum(), (x, w, gate, up, down))
+    gg = torch.autograd.grad(got.square().sum(), (x, w, gate, up, down))
+    for a, b in zip(gg, gw):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)

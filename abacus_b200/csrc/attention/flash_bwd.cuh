@@ -435,11 +435,13 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
           const float pr = valid ? ex2_approx(__uint_as_float(sv32[t]) * p.scale_log2 - lse2) : 0.f;
           const float ds = pr * (__uint_as_float(dp32[t]) - dl_);
           if (PASSES == 3) {
-            const float a = to_tf32_alu(pr), d2 = to_tf32_alu(ds);
+            float a, a_lo, d2, d2_lo;
+            split_tf32(pr, a, a_lo);
+            split_tf32(ds, d2, d2_lo);
             sv32[t] = __float_as_uint(a);
-            pl[t] = __float_as_uint(to_tf32_alu(pr - a));
+            pl[t] = __float_as_uint(a_lo);
             dp32[t] = __float_as_uint(d2);
-            dl[t] = __float_as_uint(to_tf32_alu(ds - d2));
+            dl[t] = __float_as_uint(d2_lo);
           } else {
             sv32[t] = __float_as_uint(pr);
             dp32[t] = __float_as_uint(ds);
@@ -832,9 +834,10 @@ __global__ void __maxnreg__((DqCfg<D, PASSES>::kMaxRegs)) flash_bwd_dq_kernel(co
           const float pr = valid ? ex2_approx(__uint_as_float(sv32[t]) * p.scale_log2 - lse2) : 0.f;
           const float ds = pr * (__uint_as_float(dp32[t]) - dl_);
           if (PASSES == 3) {
-            const float a = to_tf32_alu(ds);
+            float a, a_lo;
+            split_tf32(ds, a, a_lo);
             dp32[t] = __float_as_uint(a);
-            sv32[t] = __float_as_uint(to_tf32_alu(ds - a));
+            sv32[t] = __float_as_uint(a_lo);
           } else {
             dp32[t] = __float_as_uint(ds);
           }

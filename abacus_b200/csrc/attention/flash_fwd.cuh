@@ -399,9 +399,10 @@ __global__ void __maxnreg__((FwdCfg<D, PASSES>::kMaxRegs)) flash_fwd_kernel(cons
             const float e = (sv[i] == -FLT_MAX) ? 0.f : ex2_approx(sv[i] - m_new);
             bsum += e;
             if (PASSES == 3) {
-              const float hi = to_tf32_alu(e);
+              float hi, lo;
+              split_tf32(e, hi, lo);
               vh[i] = __float_as_uint(hi);
-              vl[i] = __float_as_uint(to_tf32_alu(e - hi));
+              vl[i] = __float_as_uint(lo);
             } else {
               vh[i] = __float_as_uint(e);
             }

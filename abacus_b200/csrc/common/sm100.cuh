@@ -340,6 +340,20 @@ __device__ __forceinline__ float to_tf32_alu(float x) {
   return __uint_as_float((u & 0x7f800000u) == 0x7f800000u ? u : r);
 }
 
+// The low part of a split, lo = x - hi, rounded the same way but without the
+// Inf / NaN pass-through: when x is Inf or NaN, hi already carries it into the
+// product, so the value of lo does not matter. Two integer operations.
+__device__ __forceinline__ float to_tf32_lo(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
+}
+
+// hi part on the conversion unit and lo on the integer ALUs: the two
+// halves of a softmax-loop split run on different pipes.
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  hi = to_tf32(x);
+  lo = to_tf32_lo(x - hi);
+}
+
 // 2^x on the special-function unit (ex2.approx, denormal results flushed to
 // zero). Softmax probabilities below 2^-126 are zero for training purposes.
 __device__ __forceinline__ float ex2_approx(float x) {

@@ -90,6 +90,7 @@ void ep_combine(torch::Tensor ret, c10::optional<torch::Tensor> weights, int64_t
                 int64_t target, torch::Tensor out);
 void ar_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, torch::Tensor counts, bool normalize,
               int64_t rank, int64_t lo, int64_t hi, torch::Tensor exp_avg, torch::Tensor exp_avg_sq, double lr,
-              double beta1, double beta2, double eps, double weight_decay, int64_t step, int64_t max_ctas);
+              double beta1, double beta2, double eps, double weight_decay, int64_t step, int64_t max_ctas,
+              c10::optional<torch::Tensor> local_param);
 }  // namespace comm
 }  // namespace abacus

@@ -78,8 +78,8 @@ void flash_fwd_trace(c10::optional<torch::Tensor> buf) {
     g_bwd_trace = nullptr;
     return;
   }
-  TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == torch::kInt64 && buf->is_contiguous() && buf->numel() >= 14 * 64,
-              "trace buffer: contiguous int64 CUDA tensor of >= 896 entries");
+  TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == torch::kInt64 && buf->is_contiguous() && buf->numel() >= 18 * 64,
+              "trace buffer: contiguous int64 CUDA tensor of >= 1152 entries");
   g_fwd_trace = reinterpret_cast<long long*>(buf->data_ptr<int64_t>());
   g_bwd_trace = g_fwd_trace + 9 * 64;  // the dK/dV kernel's stamps follow
 }

@@ -59,7 +59,9 @@ struct BwdParams {
   int* status;
   // Optional phase trace of the dK/dV kernel (clock64 stamps of CTA (0, 0, 0),
   // slot * 64 + block): 0 S^T / dP^T issued, 1 S^T seen by the threads,
-  // 2 P^T / dS^T written, 3 dV / dK issued, 4 partials drained.
+  // 2 P^T / dS^T written, 3 dV / dK issued, 4 partials drained, 5 K-major
+  // tiles split, 6 MN-major tiles split, 7 K-major load issued, 8 MN-major
+  // load issued.
   long long* trace;
 };
 
@@ -250,6 +252,7 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
           const int qrow = q_row_base + (block_list[step] & 0xFFFF) * NQ;
           // K-major Q / dO: free once the previous block's S^T / dP^T MMAs ran.
           if (step >= 1 && !mbar_wait(&kf_empty, (step - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+          ABACUS_BWD_TRACE(7, step)
           mbar_arrive_expect_tx(&kf_full, 2 * Cfg::kQTile);
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
@@ -263,6 +266,7 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
           const int qrow = q_row_base + (block_list[i] & 0xFFFF) * NQ;
           // MN-major Q / dO: free once the previous block's dV / dK MMAs ran.
           if (i >= 1 && !mbar_wait(&mn_empty, (i - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
+          ABACUS_BWD_TRACE(8, i)
           mbar_arrive_expect_tx(&mn_full, 2 * Cfg::kQTile);
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
@@ -548,6 +552,7 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
         split_tile(tile(2, 0), tile(2, 1), Cfg::kQTile, ct, 128);
         fence_proxy_async_smem();
         mbar_arrive(&kf_conv);
+        if (ct == 0) ABACUS_BWD_TRACE(5, step)
       }
       if (step >= 1) {
         if (!mbar_wait_warp(&mn_full, (step - 1) & 1, p.status, kStatusTimeoutFull)) break;
@@ -555,6 +560,7 @@ __global__ void __maxnreg__((DkdvCfg<D, PASSES>::kMaxRegs)) flash_bwd_dkdv_kerne
         split_tile(tile(3, 0), tile(3, 1), Cfg::kQTile, ct, 128);
         fence_proxy_async_smem();
         mbar_arrive(&mn_conv);
+        if (ct == 0) ABACUS_BWD_TRACE(6, step - 1)
       }
     }
   }

@@ -2,6 +2,7 @@
 #include <torch/extension.h>
 #include "api.h"
 #include "common/host.h"
+#include "ops/transpose.h"
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_out", &abacus::gemm::gemm_out, "tcgen05 tf32 / 3xTF32 GEMM into C");
@@ -12,6 +13,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_batched", &abacus::gemm::gemm_batched, "batched tcgen05 GEMM over (B, H, rows, cols) views");
   m.def("gemm_swiglu", &abacus::gemm::gemm_swiglu, "gate/up GEMM with SwiGLU epilogue");
   m.def("gemm_swiglu_bwd", &abacus::gemm::gemm_swiglu_bwd, "down-projection dgrad with SwiGLU backward epilogue");
+  m.def("transpose2d", &abacus::ops::transpose2d, "out = in^T (fp32, tiled)");
   m.def("rmsnorm_fwd", &abacus::ops::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &abacus::ops::rmsnorm_bwd);
   m.def("qk_prologue_fwd", &abacus::ops::qk_prologue_fwd);

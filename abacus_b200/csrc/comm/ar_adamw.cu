@@ -80,11 +80,15 @@ __global__ void symm_barrier_kernel(const __grid_constant__ PeerTable t, int ran
   __threadfence_system();
 }
 
+// With `local` set (ZeRO-3: this rank stores only its own slice of the
+// parameters), the slice is read from and written to local[i - lo4] and no
+// replica is updated on the peers: a reduce-scatter fused with the
+// partitioned AdamW update.
 __global__ void __launch_bounds__(256) ar_adamw_kernel(const __grid_constant__ PeerTable t, int rank, int world,
                                                         long long lo4, long long hi4, float* __restrict__ m,
                                                         float* __restrict__ v, float lr, float beta1, float beta2,
                                                         float eps, float wd, float bc1, float bc2_sqrt, int normalize,
-                                                        int* status) {
+                                                        float* __restrict__ local, int* status) {
   if (*reinterpret_cast<volatile int*>(status) != kStatusOk) return;
   const float decay = 1.f - lr * wd;
   const float step_size = lr / bc1;
@@ -101,7 +105,8 @@ __global__ void __launch_bounds__(256) ar_adamw_kernel(const __grid_constant__ P
   const float inv_total = !normalize ? 1.f : (total > 0.f ? 1.f / total : 0.f);
 #pragma unroll
   for (int p = 0; p < kMaxPeers; ++p) weight[p] *= inv_total;
-  const float4* params = reinterpret_cast<const float4*>(t.param[rank]);
+  const float4* params = local ? reinterpret_cast<const float4*>(local) - lo4
+                                : reinterpret_cast<const float4*>(t.param[rank]);
   float4* m4 = reinterpret_cast<float4*>(m);
   float4* v4 = reinterpret_cast<float4*>(v);
   for (long long i = lo4 + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < hi4;
@@ -133,9 +138,13 @@ __global__ void __launch_bounds__(256) ar_adamw_kernel(const __grid_constant__ P
     upd(wv.w, mv.w, vv.w, g.w);
     m4[i - lo4] = mv;
     v4[i - lo4] = vv;
+    if (local) {
+      reinterpret_cast<float4*>(local)[i - lo4] = wv;
+    } else {
 #pragma unroll
-    for (int p = 0; p < kMaxPeers; ++p) {
-      if (p < world) reinterpret_cast<float4*>(t.param[p])[i] = wv;
+      for (int p = 0; p < kMaxPeers; ++p) {
+        if (p < world) reinterpret_cast<float4*>(t.param[p])[i] = wv;
+      }
     }
   }
   __threadfence_system();
@@ -190,7 +199,8 @@ void symm_barrier(std::vector<int64_t> signal_ptrs, int64_t rank, int64_t slot_b
 
 void ar_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, torch::Tensor counts,
               bool normalize, int64_t rank, int64_t lo, int64_t hi, torch::Tensor exp_avg, torch::Tensor exp_avg_sq,
-              double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step, int64_t max_ctas) {
+              double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step, int64_t max_ctas,
+              c10::optional<torch::Tensor> local_param) {
   const c10::cuda::CUDAGuard guard(exp_avg.device());
   TORCH_CHECK(lo % 4 == 0 && hi % 4 == 0 && hi >= lo, "owned range must be float4 aligned");
   TORCH_CHECK(exp_avg.is_contiguous() && exp_avg_sq.is_contiguous() && exp_avg.numel() == hi - lo &&
@@ -200,6 +210,15 @@ void ar_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, t
                   counts.numel() == static_cast<int64_t>(grad_ptrs.size()),
               "counts must be a 1-D float32 CUDA tensor with one entry per rank");
   TORCH_CHECK(rank >= 0 && rank < static_cast<int64_t>(grad_ptrs.size()), "rank out of range");
+  float* local = nullptr;
+  if (local_param) {
+    TORCH_CHECK(local_param->is_cuda() && local_param->scalar_type() == torch::kFloat32 &&
+                    local_param->is_contiguous() && local_param->numel() == hi - lo &&
+                    reinterpret_cast<uintptr_t>(local_param->data_ptr()) % 16 == 0,
+                "local_param: the owned slice, contiguous fp32, 16-byte aligned");
+    local = local_param->data_ptr<float>();
+    param_ptrs.assign(grad_ptrs.size(), 0);  // no replica to update
+  }
   std::vector<int64_t> dummy(grad_ptrs.size(), 0);
   PeerTable t = make_table(grad_ptrs, param_ptrs, dummy, {});
   t.counts = counts.data_ptr<float>();
@@ -216,7 +235,7 @@ void ar_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, t
   ar_adamw_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       t, static_cast<int>(rank), static_cast<int>(grad_ptrs.size()), lo / 4, hi / 4, exp_avg.data_ptr<float>(),
       exp_avg_sq.data_ptr<float>(), static_cast<float>(lr), static_cast<float>(beta1), static_cast<float>(beta2),
-      static_cast<float>(eps), static_cast<float>(weight_decay), bc1, bc2s, normalize ? 1 : 0,
+      static_cast<float>(eps), static_cast<float>(weight_decay), bc1, bc2s, normalize ? 1 : 0, local,
       host::status_ptr(exp_avg.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   host::note_launch();

@@ -293,7 +293,7 @@ class FusedDataParallel(DataParallel):
                 self._grad_ptrs, self._param_ptrs, self._exch_counts[:, 0], self.token_weighted, self.rank, b.lo, b.hi,
                 self._exp_avg[b.moment_off : b.moment_off + b.slice],
                 self._exp_avg_sq[b.moment_off : b.moment_off + b.slice], lr, beta1, beta2, eps, wd, step,
-                self.reduce_ctas if self.overlap else 0,
+                self.reduce_ctas if self.overlap else 0, None,
             )
         b.launched = True
         self._next_bucket += 1

@@ -5,8 +5,10 @@ QK-norm, vocab 50304, untied embeddings, fp32 parameters. Data: synthetic
 uniform-random int64 tokens (seed 0), seq_len 1024, global batch 64
 sequences (64 / N per rank; strong scaling). Data parallel for N > 1, one
 process per GPU: by default the fused peer-memory gradient reduce + AdamW +
-parameter broadcast kernel (``--dp fused``); ``--dp nccl`` runs bucketed NCCL
-all-reduce + AdamW and ``--dp zero3`` ZeRO-3 on NCCL.
+parameter broadcast kernels under backward (``--dp fused``); ``--dp nccl``
+runs bucketed NCCL all-reduce + AdamW, ``--dp zero3`` ZeRO-3 with NVLink push
+all-gathers and a fused reduce-scatter + AdamW, ``--dp zero3-nccl`` ZeRO-3 on
+NCCL.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl abacus|reference]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
@@ -57,9 +59,10 @@ def parse_args():
     p.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
     p.add_argument("--seq-len", type=int, default=SEQ_LEN)
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--dp", choices=("fused", "nccl", "zero3"), default="fused",
-                   help="N>1: fused peer-memory reduce+AdamW kernel, NCCL bucketed all-reduce + AdamW, "
-                        "or ZeRO-3 / FSDP (NCCL)")
+    p.add_argument("--dp", choices=("fused", "nccl", "zero3", "zero3-nccl"), default="fused",
+                   help="N>1: fused peer-memory reduce+AdamW kernel under backward, NCCL bucketed all-reduce + "
+                        "AdamW, ZeRO-3 / FSDP with push all-gathers and a fused reduce-scatter + AdamW, or "
+                        "ZeRO-3 on NCCL")
     return p.parse_args()
 
 
@@ -165,7 +168,7 @@ def timed_steps(step_fn, batches, steps, world, device):
 def build_abacus(args, world, device):
     sys.path.insert(0, ROOT)
     from abacus_b200.ops import precision
-    from abacus_b200.distributed.data_parallel import DataParallel, FusedDataParallel
+    from abacus_b200.distributed.data_parallel import DataParallel, FusedDataParallel, FusedZero3
     from abacus_b200.trainer import Trainer
     from abacus_b200.transformer import Transformer
 
@@ -177,8 +180,10 @@ def build_abacus(args, world, device):
         model = model.to(device)
         if args.dp == "fused":
             parallel = FusedDataParallel(model)
+        elif args.dp == "zero3":
+            parallel = FusedZero3(model)
         else:
-            parallel = DataParallel(model, stage=3 if args.dp == "zero3" else 0)
+            parallel = DataParallel(model, stage=3 if args.dp == "zero3-nccl" else 0)
     trainer = Trainer(model, parallel, total_steps=args.warmup + 2 * args.steps + 2)
     return trainer
 
@@ -187,7 +192,7 @@ def build_reference(args, world, device):
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "abacus")):
         return None, "reference not installed in baseline/_ref"
-    if world > 1 and args.dp == "zero3":
+    if world > 1 and args.dp in ("zero3", "zero3-nccl"):
         return None, ("the reference's ZeRO-3 calls dist.all_gather_single / reduce_scatter_single, "
                       "which torch 2.11 does not provide")
     sys.path.insert(0, ref)
@@ -291,12 +296,15 @@ def main():
                 "model": "dense GPT ~125M: 12L d768 12x64 heads, SwiGLU 2048, RoPE, QK-norm, vocab 50304",
                 "global_batch": args.global_batch,
                 "seq_len": args.seq_len,
-                "parallelism": (f"zero3-dp{world}" if args.dp == "zero3" else f"dp{world}") if world > 1 else "single",
+                "parallelism": (f"zero3-dp{world}" if args.dp.startswith("zero3") else f"dp{world}")
+                if world > 1 else "single",
                 "dp_comm": None if world == 1 else (
-                    "fused NVLink peer-memory gradient reduce + AdamW + broadcast kernel"
+                    "fused NVLink peer-memory gradient reduce + AdamW + broadcast per bucket under backward"
                     if impl == "abacus" and args.dp == "fused"
-                    else ("NCCL all-gather / reduce-scatter per unit (ZeRO-3)" if args.dp == "zero3"
-                          else "NCCL all-reduce, then AdamW")),
+                    else ("NVLink push all-gather per unit + fused reduce-scatter / AdamW under backward (ZeRO-3)"
+                          if impl == "abacus" and args.dp == "zero3"
+                          else ("NCCL all-gather / reduce-scatter per unit (ZeRO-3)" if args.dp == "zero3-nccl"
+                                else "NCCL all-reduce, then AdamW"))),
                 "l2": "inputs/activations larger than L2 (no flush needed)",
                 "compute": "3xTF32 split precision on tcgen05 (fp32 accuracy)" if args.precision == "fp32" and impl == "abacus"
                 else ("tf32 tcgen05" if impl == "abacus" else "reference: torch fp32 (TF32 off)"),

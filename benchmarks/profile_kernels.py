@@ -122,7 +122,7 @@ def run(name):
             counts = torch.ones(1, device=dev)
             ptrs = [[t.data_ptr()] for t in flat]
             ms = timed(lambda: ext().ar_adamw(ptrs[0], ptrs[1], counts, True, 0, 0, n, m, v, 1e-3, 0.9, 0.999, 1e-8,
-                                              0.01, 1, 0))
+                                              0.01, 1, 0, None))
             return ms, 7 * n * 4 / ms / 1e6, "GB/s (grad, param, m, v read; param, m, v written)"
         from abacus_b200.parallel import tp_fused
 

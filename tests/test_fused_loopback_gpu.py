@@ -177,7 +177,7 @@ def test_data_parallel_reduce_adamw_broadcast():
     for step in (1, 2):
         for r in range(WORLD):
             ext().ar_adamw([g.data_ptr() for g in grads], [p.data_ptr() for p in params], counts, True, r,
-                           r * half, (r + 1) * half, moments[r][0], moments[r][1], lr, b1, b2, eps, wd, step, 0)
+                           r * half, (r + 1) * half, moments[r][0], moments[r][1], lr, b1, b2, eps, wd, step, 0, None)
     torch.cuda.synchronize()
     check_status()
     # Oracle: two AdamW steps on the token-weighted mean gradient.
@@ -190,3 +190,29 @@ def test_data_parallel_reduce_adamw_broadcast():
         w = w - lr / (1 - b1**step) * m / ((v / (1 - b2**step)).sqrt() + eps)
     assert torch.equal(params[0], params[1])
     assert _rel(params[0], w) < 1e-6
+
+
+def test_zero3_reduce_scatter_adamw_into_local_slices():
+    """ZeRO-3 variant: rank r reduces its slice of both ranks' gradients and
+    updates only its own locally stored slice (no replica is written)."""
+    torch.manual_seed(4)
+    n = 4096 * 2
+    half = n // WORLD
+    grads = [torch.randn(n, device="cuda") for _ in range(WORLD)]
+    w0 = torch.randn(n, device="cuda")
+    slices = [w0[r * half : (r + 1) * half].clone() for r in range(WORLD)]
+    moments = [(torch.zeros(half, device="cuda"), torch.zeros(half, device="cuda")) for _ in range(WORLD)]
+    counts = torch.tensor([100.0, 300.0], device="cuda")
+    lr, b1, b2, eps, wd = 2e-3, 0.9, 0.95, 1e-8, 0.1
+    dummy = [0] * WORLD
+    for r in range(WORLD):
+        ext().ar_adamw([g.data_ptr() for g in grads], dummy, counts, True, r, r * half, (r + 1) * half,
+                       moments[r][0], moments[r][1], lr, b1, b2, eps, wd, 1, 0, slices[r])
+    torch.cuda.synchronize()
+    check_status()
+    g = (grads[0].double() * 100 + grads[1].double() * 300) / 400
+    w = w0.double() * (1 - lr * wd)
+    m = (1 - b1) * g
+    v = (1 - b2) * g * g
+    w = w - lr / (1 - b1) * m / ((v / (1 - b2)).sqrt() + eps)
+    assert _rel(torch.cat(slices), w) < 1e-6

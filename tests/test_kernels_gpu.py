@@ -139,3 +139,14 @@ def test_multi_tensor_adamw_matches_reference_sequence():
     for p, c in zip(params, cpu):
         _close(p.detach().cpu(), c.detach(), 1e-6)
         _close(opt.state[id(p)]["exp_avg_sq"].cpu(), ref.state[id(c)]["exp_avg_sq"], 1e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,cols", [(65536, 768), (333, 130), (64, 64), (7, 1)])
+def test_transpose_kernel(rows, cols):
+    from abacus_b200.ops import gemm
+
+    x = torch.randn(rows, cols, device="cuda")
+    assert torch.equal(gemm.transpose(x), x.t())
+    view = torch.randn(rows, cols + 3, device="cuda")[:, 1 : cols + 1]  # unaligned, strided rows
+    assert torch.equal(gemm.transpose(view), view.t())

@@ -2,17 +2,21 @@
 #include <torch/extension.h>
 #include "api.h"
 #include "common/host.h"
+#include "ops/router.h"
 #include "ops/transpose.h"
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_out", &abacus::gemm::gemm_out, "tcgen05 tf32 / 3xTF32 GEMM into C");
   m.def("gemm_n_tiles", &abacus::gemm::gemm_n_tiles, "N tiles of a single-B GEMM of the given output width");
+  m.def("gemm_pair_clusters", &abacus::gemm::gemm_pair_clusters, "CTA pairs of the last CTA-pair GEMM launch");
   m.def("gemm_out_tp", &abacus::gemm::gemm_out_tp, "GEMM with a peer-gathered operand and/or row-scattered output");
   m.def("gemm_swiglu_tp", &abacus::gemm::gemm_swiglu_tp, "SwiGLU up-projection over a peer-gathered input");
   m.def("gemm_swiglu_bwd_tp", &abacus::gemm::gemm_swiglu_bwd_tp, "SwiGLU backward GEMM over a peer-gathered dy");
   m.def("gemm_batched", &abacus::gemm::gemm_batched, "batched tcgen05 GEMM over (B, H, rows, cols) views");
   m.def("gemm_swiglu", &abacus::gemm::gemm_swiglu, "gate/up GEMM with SwiGLU epilogue");
   m.def("gemm_swiglu_bwd", &abacus::gemm::gemm_swiglu_bwd, "down-projection dgrad with SwiGLU backward epilogue");
+  m.def("router_logits", &abacus::ops::router_logits, "MoE router scores x @ w (E <= 64)");
+  m.def("router_logits_bwd", &abacus::ops::router_logits_bwd, "gradients of the router scores");
   m.def("transpose2d", &abacus::ops::transpose2d, "out = in^T (fp32, tiled)");
   m.def("rmsnorm_fwd", &abacus::ops::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &abacus::ops::rmsnorm_bwd);

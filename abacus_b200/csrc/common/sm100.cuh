@@ -115,6 +115,38 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, i
   return __all_sync(0xffffffffu, ok);
 }
 
+// ---------------------------------------------------------------- CTA pairs
+// Two CTAs of a (2, 1, 1) cluster on neighbouring SMs share one tcgen05 MMA
+// (cta_group::2): each holds half of A's rows (and of D) and half of B's
+// columns, so every SM reads only its half of B from its own shared memory.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// Arrive on a barrier of any CTA of the cluster (default semantics: release
+// at CTA scope; a release at cluster scope costs a memory barrier per arrive
+// (measured: membar stalls took the pair GEMM below the single-CTA one). The
+// data the arrive publishes is ordered by the async-proxy fences the callers
+// issue first: fence.proxy.async for shared-memory writes and
+// tcgen05.wait::st + tcgen05.fence::before_thread_sync for TMEM.)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// All threads of both CTAs (release / acquire at cluster scope).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- peer flags
 __device__ __forceinline__ int ld_acquire_sys(const int* p) {
   int v;
@@ -206,6 +238,43 @@ __device__ __forceinline__ void tmem_relinquish() {
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Pair TMEM allocation: one warp of EACH CTA of the pair issues it (same
+// warp index, same shared-memory slot); both receive the same address.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Pair MMA, kind::tf32, issued by one thread of the even CTA: D (both CTAs'
+// TMEM, 128 lanes each) (+)= A (both CTAs' TMEM at a_tmem) * B (both CTAs'
+// shared memory at the descriptor's offset: columns [0, N/2) in the even CTA,
+// [N/2, N) in the odd one).
+__device__ __forceinline__ void mma_tf32_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
+// Arrive once on the barrier at `cluster_addr` (this CTA's or the peer's,
+// from mapa_shared) when every pair MMA issued so far by this thread is done.
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
+               : "memory");
 }
 
 // D(tmem) (+)= A(smem) * B(smem), kind::tf32, issued by a single thread.

@@ -1,5 +1,6 @@
 // Host side of the tcgen05 tf32 GEMM: tensor-map encoding, tile-config
 // selection and the torch bindings used by abacus_b200.ops.linear.
+#include <cstdlib>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -129,6 +130,24 @@ unsigned tile_grid(Params& p, long long units, int device) {
   return static_cast<unsigned>(std::min<long long>(units, sms));
 }
 
+// 3xTF32 GEMMs with at least two 128-row tiles run on CTA pairs (cta_group::2:
+// one MMA over 256 rows, each SM reads half of B), unless the launch waits for
+// peer rows or scatters its output (those keep one tile per CTA).
+// ABACUS_GEMM_PAIR=0 turns pairs off.
+bool pair_enabled() {
+  const char* e = std::getenv("ABACUS_GEMM_PAIR");
+  return !(e != nullptr && e[0] == '0');
+}
+
+bool use_pair(int64_t passes, long long m, bool comm) { return pair_enabled() && passes == 3 && !comm && m >= 2 * BM; }
+
+// Persistent grid of CTA pairs for `units` 256-row work units.
+unsigned pair_grid(Params& p, long long units, int device) {
+  const int sms = at::cuda::getDeviceProperties(device)->multiProcessorCount;
+  p.persistent = 1;
+  return static_cast<unsigned>(2 * std::max<long long>(1, std::min<long long>(units, sms / 2)));
+}
+
 // Tensor-parallel options of one GEMM launch (see Params in gemm_tcgen05.cuh).
 //   wait    = [flags_ptr, operand (0 A / 1 B), epoch, chunk, seq, self]
 //   scatter = [chunk, seq, base_0..base_{P-1}, counter_0..counter_{P-1}]
@@ -201,6 +220,8 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
   (void)gemm_out_impl(c, a, bs, trans_a, trans_b, b_mode, alpha, residual, accumulate, passes, Comm{});
 }
 
+int64_t gemm_pair_clusters() { return last_pair_clusters(); }
+
 // Number of N tiles a single-B GEMM of output width n uses (stores per row).
 int64_t gemm_n_tiles(int64_t n, int64_t passes) {
   check_passes(passes);
@@ -266,10 +287,11 @@ int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tenso
   if (b_mode == kBSegN && seg % BN != 0) BN = 128;
   if (b_mode == kBSegN) TORCH_CHECK(seg % BN == 0, "segment width ", seg, " must be a multiple of the N tile ", BN);
   if (b_mode == kBSegK) TORCH_CHECK(seg % BK == 0, "segment depth must be a multiple of ", BK);
+  const bool pair = use_pair(passes, M, !cm.wait.empty() || scatter);
   Params p;
   memset(&p, 0, sizeof(p));
   p.tma_a = map_for(A, BM);
-  for (size_t i = 0; i < B.size(); ++i) p.tma_b[i] = map_for(B[i], BN);
+  for (size_t i = 0; i < B.size(); ++i) p.tma_b[i] = map_for(B[i], pair ? BN / 2 : BN);
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
@@ -288,18 +310,19 @@ int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tenso
   p.status = host::status_ptr(a.device().index());
   apply_comm(p, cm, A.mn_major, B[0].mn_major);
   const long long tiles = ((M + BM - 1) / BM) * p.num_n_tiles;
+  // Work units: 128-row tiles, or 256-row tiles of a CTA pair.
+  const long long units = pair ? ((M + 2 * BM - 1) / (2 * BM)) * p.num_n_tiles : tiles;
   const int k_tiles = static_cast<int>((K + BK - 1) / BK);
   const int sms = at::cuda::getDeviceProperties(a.device().index())->multiProcessorCount;
-  int splits = (N % 4 == 0 && !scatter) ? pick_splits(tiles, k_tiles, sms) : 1;
+  int splits = (N % 4 == 0 && !scatter) ? pick_splits(units, k_tiles, pair ? sms / 2 : sms) : 1;
   auto stream = at::cuda::getCurrentCUDAStream();
   p.k_tiles_per_split = (k_tiles + splits - 1) / splits;
   splits = (k_tiles + p.k_tiles_per_split - 1) / p.k_tiles_per_split;
   if (splits == 1) {
     p.splits = 1;
     p.batch_z = 1;
-    const unsigned gx = tile_grid(p, tiles, a.device().index());
-    launch_store(p, dim3(gx, 1), BN, A.mn_major, B[0].mn_major, static_cast<int>(passes),
-                 stream);
+    const unsigned gx = pair ? pair_grid(p, units, a.device().index()) : tile_grid(p, tiles, a.device().index());
+    launch_store(p, dim3(gx, 1), BN, A.mn_major, B[0].mn_major, static_cast<int>(passes), stream, pair);
     if (!scatter) return 0;
     if (cm.scatter[0] == -1) return p.num_n_tiles;  // each row lands once per N tile
     const int64_t owners = (static_cast<int64_t>(cm.scatter.size()) - 2) / 2;
@@ -318,9 +341,9 @@ int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tenso
   q.accumulate = 0;
   q.splits = splits;
   q.batch_z = 1;
-  const unsigned gxs = tile_grid(q, tiles * splits, a.device().index());
-  launch_store(q, dim3(gxs, 1), BN, A.mn_major, B[0].mn_major,
-               static_cast<int>(passes), stream);
+  const unsigned gxs = pair ? pair_grid(q, units * splits, a.device().index())
+                           : tile_grid(q, tiles * splits, a.device().index());
+  launch_store(q, dim3(gxs, 1), BN, A.mn_major, B[0].mn_major, static_cast<int>(passes), stream, pair);
   const long long items = M * (N / 4);
   splitk_reduce_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, stream>>>(
       ws.data_ptr<float>(), splits, M, N, p.alpha, p.r, p.ldr, p.accumulate, p.c, p.ldc);
@@ -457,12 +480,14 @@ void gemm_swiglu_impl(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up,
   p.status = host::status_ptr(x.device().index());
   apply_comm(p, cm, false, true);
   p.k_tiles_per_split = static_cast<int>((A.k + BK - 1) / BK);
+  const bool pair = use_pair(passes, T, !cm.wait.empty());
   const long long tiles = ((T + BM - 1) / BM) * p.num_n_tiles;
+  const long long units = ((T + 2 * BM - 1) / (2 * BM)) * p.num_n_tiles;
   p.splits = 1;
   p.batch_z = 1;
-  const unsigned grid = tile_grid(p, tiles, x.device().index());
+  const unsigned grid = pair ? pair_grid(p, units, x.device().index()) : tile_grid(p, tiles, x.device().index());
   auto stream = at::cuda::getCurrentCUDAStream();
-  launch_swiglu(p, dim3(grid, 1), BN, static_cast<int>(passes), stream);
+  launch_swiglu(p, dim3(grid, 1), BN, static_cast<int>(passes), stream, pair);
 }
 }  // namespace
 
@@ -492,10 +517,11 @@ void gemm_swiglu_bwd_impl(torch::Tensor dy, torch::Tensor w_down, torch::Tensor 
   TORCH_CHECK(dgu.size(0) == T && dgu.size(1) == 2 * Mh, "dgu must be (T, 2*hidden)");
   if (T == 0 || Mh == 0) return;
   const int BN = passes == 3 ? 128 : (Mh >= 2048 ? 256 : 128);
+  const bool pair = use_pair(passes, T, !cm.wait.empty());
   Params p;
   memset(&p, 0, sizeof(p));
   p.tma_a = map_for(A, BM);
-  p.tma_b[0] = map_for(B, BN);
+  p.tma_b[0] = map_for(B, pair ? BN / 2 : BN);
   p.M = static_cast<int>(T);
   p.N = static_cast<int>(Mh);
   p.K = static_cast<int>(A.k);
@@ -511,11 +537,12 @@ void gemm_swiglu_bwd_impl(torch::Tensor dy, torch::Tensor w_down, torch::Tensor 
   apply_comm(p, cm, false, false);
   p.k_tiles_per_split = static_cast<int>((A.k + BK - 1) / BK);
   const long long tiles = ((T + BM - 1) / BM) * p.num_n_tiles;
+  const long long units = ((T + 2 * BM - 1) / (2 * BM)) * p.num_n_tiles;
   p.splits = 1;
   p.batch_z = 1;
-  const unsigned grid = tile_grid(p, tiles, dy.device().index());
+  const unsigned grid = pair ? pair_grid(p, units, dy.device().index()) : tile_grid(p, tiles, dy.device().index());
   auto stream = at::cuda::getCurrentCUDAStream();
-  launch_swiglu_bwd(p, dim3(grid, 1), BN, static_cast<int>(passes), stream);
+  launch_swiglu_bwd(p, dim3(grid, 1), BN, static_cast<int>(passes), stream, pair);
 }
 }  // namespace
 

@@ -116,10 +116,14 @@ __device__ __forceinline__ bool wait_gathered_rows(const Params& p, int r0, int 
   return true;
 }
 
-template <int BN, bool A_MN, bool B_MN, int PASSES, int STAGES>
+template <int BN, bool A_MN, bool B_MN, int PASSES, int STAGES, bool PAIR = false>
 struct Config {
+  // CTA pair (cta_group::2, 3xTF32 only): the pair computes a 256 x BN tile;
+  // each CTA holds its 128 rows of A and BN / 2 columns of B.
+  static_assert(!PAIR || PASSES == 3, "CTA pairs are built for the 3xTF32 mode");
+  static constexpr int kBCols = PAIR ? BN / 2 : BN;  // B columns in this CTA's shared memory
   static constexpr int kABytes = BM * BK * 4;
-  static constexpr int kBBytes = BN * BK * 4;
+  static constexpr int kBBytes = kBCols * BK * 4;
   // 3xTF32 stage: A landing buffer, B hi (in place), B lo. A hi / lo live in
   // TMEM (written by the converter), so the MMA reads A without touching smem.
   static constexpr int kStageBytes = PASSES == 3 ? kABytes + 2 * kBBytes : kABytes + kBBytes;
@@ -130,18 +134,22 @@ struct Config {
   static constexpr bool kChunked = PASSES == 3;
   static constexpr int kChunk = 2;
   static constexpr int kATmem = 2 * BN;  // first TMEM column of the A stages (3xTF32)
+  // A hi / lo stages in TMEM (3xTF32): at most 4 fit beside the two 128-column
+  // accumulators, so shared-memory stages beyond that (CTA pairs: 6) are
+  // recycled through their own release barriers.
+  static constexpr int kAStages = STAGES < 4 ? STAGES : 4;
   // 1 pass: two accumulator buffers, so a persistent CTA's epilogue of one
   // tile overlaps the MMAs of the next.
-  static constexpr int kAccCols = kChunked ? 2 * BN + STAGES * 2 * BK : 2 * BN;
+  static constexpr int kAccCols = kChunked ? 2 * BN + kAStages * 2 * BK : 2 * BN;
   static constexpr uint32_t kTmemCols = kAccCols <= 32 ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
 };
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
-template <int BN, bool A_MN, bool B_MN, int PASSES, int EPI, int STAGES>
-__global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThreads, 1)
+template <int BN, bool A_MN, bool B_MN, int PASSES, int EPI, int STAGES, bool PAIR = false>
+__global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::kThreads, 1)
     gemm_kernel(const __grid_constant__ Params p) {
-  using Cfg = Config<BN, A_MN, B_MN, PASSES, STAGES>;
+  using Cfg = Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full_bar[STAGES];
   __shared__ uint64_t empty_bar[STAGES];
@@ -150,16 +158,25 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   __shared__ uint64_t accum_empty[2];
   __shared__ uint64_t chunk_full[2];
   __shared__ uint64_t chunk_empty[2];
+  __shared__ uint64_t a_empty[4];  // 3xTF32: TMEM A stage released by the MMAs
   __shared__ uint32_t tmem_base_slot;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   // Abort early (uniformly for the whole CTA) if an earlier kernel on this
   // device already recorded an error.
+  // (A pair never returns early: both CTAs must reach the pair TMEM
+  // allocation and the closing cluster barrier; after an earlier error its
+  // bounded waits end at once instead.)
   __shared__ int abort_flag;
   if (threadIdx.x == 0) abort_flag = *reinterpret_cast<volatile int*>(p.status);
   __syncthreads();
-  if (abort_flag != kStatusOk) return;
+  if (!PAIR && abort_flag != kStatusOk) return;
+  // Pair role: rank 0 issues the MMAs for both CTAs.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  // Shared-memory address of barrier `bar` in the pair's MMA-issuing CTA.
+  auto leader_addr = [&](uint64_t* bar) { return mapa_shared(smem_u32(bar), 0); };
 
   // 1024-byte aligned stage buffers (swizzle period of SWIZZLE_128B).
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -172,13 +189,17 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
   // blockIdx.x + gridDim.x, ...; stage, chunk and accumulator phases run on
   // across tiles, so the epilogue of one tile overlaps the MMAs of the next.
   // Tiles are grouped along M for L2 reuse of B.
-  const int num_m_tiles = (p.M + BM - 1) / BM;
+  // A pair walks 256-row tiles (rows [m0, m0 + 128) in rank 0, the next 128
+  // in rank 1) with cluster index blockIdx.x / 2.
+  constexpr int kTileM = PAIR ? 2 * BM : BM;
+  const int num_m_tiles = (p.M + kTileM - 1) / kTileM;
   const int num_n_tiles = p.num_n_tiles;
   const int total_tiles = num_m_tiles * num_n_tiles;
   const int n_splits = max(1, p.splits);
   const int n_z = max(1, p.batch_z);
   const int total_units = total_tiles * n_splits * n_z;
-  const int unit_step = p.persistent ? static_cast<int>(gridDim.x) : total_units;
+  const int first_unit = PAIR ? static_cast<int>(blockIdx.x / 2) : static_cast<int>(blockIdx.x);
+  const int unit_step = PAIR ? static_cast<int>(gridDim.x / 2) : (p.persistent ? static_cast<int>(gridDim.x) : total_units);
   constexpr int kGroup = 16;
   struct TileInfo {
     int m0, n0, kt_begin, num_k;
@@ -197,7 +218,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     const int first_m = group * kGroup;
     const int group_m = min(num_m_tiles - first_m, kGroup);
     const int in_group = tile - group * kGroup * num_n_tiles;
-    t.m0 = (first_m + in_group % group_m) * BM;
+    t.m0 = (first_m + in_group % group_m) * kTileM + static_cast<int>(rank) * BM;
     // Output column base. For SwiGLU forward a tile covers BN/2 hidden units.
     t.n0 = (in_group / group_m) * (EPI == kEpiSwiGLU ? BN / 2 : BN);
     t.skip = p.causal == 1 && t.n0 >= t.m0 + BM;  // fully masked tile
@@ -209,9 +230,9 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     t.num_k = max(0, min(total_k, t.kt_begin + p.k_tiles_per_split) - t.kt_begin);
     return t;
   };
-  if (!p.persistent && tile_at(blockIdx.x).skip) return;  // uniform exit
+  if (!PAIR && !p.persistent && tile_at(blockIdx.x).skip) return;  // uniform exit
   int cur_h = 0, cur_b = 0;  // batched matrix of the tile being loaded (producer)
-  if (p.wait_flags != nullptr) {
+  if (!PAIR && p.wait_flags != nullptr) {
     // (Never persistent.) Rows of the gathered operand this CTA reads: the M
     // range for a K-major A, else the K range (MN-major A or B store tokens
     // along K).
@@ -240,18 +261,22 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     else tma_load_2d(dst, map, bar, x, y);
   };
 
+  // In a pair the converter and epilogue warps of both CTAs arrive once per
+  // warp on the leader's conv_bar / chunk_empty (8 arrivals).
+  constexpr uint32_t kWarpArrivals = PAIR ? 8 : 128;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
-      mbar_init(&conv_bar[s], 128);
+      mbar_init(&conv_bar[s], kWarpArrivals);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accum_full[b], 1);
       mbar_init(&accum_empty[b], 128);
       mbar_init(&chunk_full[b], 1);
-      mbar_init(&chunk_empty[b], 128);
+      mbar_init(&chunk_empty[b], kWarpArrivals);
     }
+    for (int s = 0; s < 4; ++s) mbar_init(&a_empty[s], 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -259,11 +284,19 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     tma_prefetch_desc(&p.tma_b[0]);
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_base_slot, Cfg::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(&tmem_base_slot, Cfg::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&tmem_base_slot, Cfg::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  // A pair also needs the other CTA's barriers initialised before any remote
+  // arrive: synchronise the whole cluster.
+  if constexpr (PAIR) cluster_sync_all();
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_slot;
 
@@ -272,7 +305,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     if (elect_one_sync()) {
       int issued = 0;  // k-tiles issued over all tiles of this CTA
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_units && ok; tile += unit_step) {
+      for (int tile = first_unit; tile < total_units && ok; tile += unit_step) {
         const TileInfo t = tile_at(tile);
         if (t.skip) continue;
         const int m0 = t.m0, n0 = t.n0;
@@ -293,20 +326,26 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
           } else {
             load(stage_a(s), &p.tma_a, &full_bar[s], k0, m0);
           }
-          // B source for this (n, k) tile.
+          // B source for this (n, k) tile. A pair's CTA loads columns
+          // [rank * BN / 2, (rank + 1) * BN / 2) of the tile; for the paired
+          // gate|up tile that is the gate half in rank 0 and the up half in rank 1.
           const CUtensorMap* bmap = &p.tma_b[0];
-          int bn = n0, bk = k0;
+          int bn = n0 + static_cast<int>(rank) * (BN / 2) * (PAIR && p.b_mode != kBDualN ? 1 : 0), bk = k0;
           if (p.b_mode == kBSegN) {
-            const int sidx = n0 / p.seg;
+            const int sidx = bn / p.seg;
             bmap = &p.tma_b[sidx];
-            bn = n0 - sidx * p.seg;
+            bn = bn - sidx * p.seg;
           } else if (p.b_mode == kBSegK) {
             const int sidx = k0 / p.seg;
             bmap = &p.tma_b[sidx];
             bk = k0 - sidx * p.seg;
           }
           if (B_MN) {
-            if (p.b_mode == kBDualN) {
+            if (p.b_mode == kBDualN && PAIR) {
+  #pragma unroll
+              for (int c = 0; c < BN / 64; ++c)
+                load(stage_b(s) + c * 32 * BK * 4, &p.tma_b[rank], &full_bar[s], n0 + 32 * c, k0);
+            } else if (p.b_mode == kBDualN) {
   #pragma unroll
               for (int c = 0; c < BN / 64; ++c) {
                 load(stage_b(s) + c * 32 * BK * 4, &p.tma_b[0], &full_bar[s], n0 + 32 * c, k0);
@@ -314,10 +353,14 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
               }
             } else {
   #pragma unroll
-              for (int c = 0; c < BN / 32; ++c) load(stage_b(s) + c * 32 * BK * 4, bmap, &full_bar[s], bn + 32 * c, bk);
+              for (int c = 0; c < Cfg::kBCols / 32; ++c)
+                load(stage_b(s) + c * 32 * BK * 4, bmap, &full_bar[s], bn + 32 * c, bk);
             }
           } else {
-            if (p.b_mode == kBDualN) {
+            // K-major B boxes are kBCols rows (BN / 2 for the paired halves).
+            if (p.b_mode == kBDualN && PAIR) {
+              load(stage_b(s), &p.tma_b[rank], &full_bar[s], k0, n0);
+            } else if (p.b_mode == kBDualN) {
               load(stage_b(s), &p.tma_b[0], &full_bar[s], k0, n0);
               load(stage_b(s) + (BN / 2) * BK * 4, &p.tma_b[1], &full_bar[s], k0, n0);
             } else {
@@ -331,17 +374,35 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
       for (int it = max(0, issued - STAGES); it < issued; ++it) {
         mbar_wait(&full_bar[it % STAGES], (it / STAGES) & 1, nullptr, 0);
       }
+      // In a pair, the leader's last commits also arrive here: let them land
+      // before this CTA can leave.
+      if (PAIR) {
+        for (int it = max(0, issued - STAGES); it < issued; ++it) {
+          if (!mbar_wait(&empty_bar[it % STAGES], (it / STAGES) & 1, p.status, kStatusTimeoutEmpty)) break;
+        }
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (elect_one_sync()) {
+    // (In a pair only rank 0 issues; its MMAs span both CTAs.)
+    if (leader && elect_one_sync()) {
       // 3xTF32 reads A from TMEM, which is always K-major (lane = row).
-      constexpr uint32_t idesc = idesc_tf32(BM, BN, PASSES == 3 ? false : A_MN, B_MN);
+      constexpr uint32_t idesc = idesc_tf32(PAIR ? 2 * BM : BM, BN, PASSES == 3 ? false : A_MN, B_MN);
+      auto wait_in = [&](uint64_t* bar, uint32_t parity, int code) { return mbar_wait(bar, parity, p.status, code); };
+      // Commit to this barrier in every CTA of the pair.
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          mma_commit_pair(smem_u32(bar));
+          mma_commit_pair(mapa_shared(smem_u32(bar), 1));
+        } else {
+          mma_commit(bar);
+        }
+      };
       int it = 0;        // k-tiles consumed over all tiles
       int chunk0 = 0;    // K chunks issued before this tile (3xTF32)
       int tcount = 0;    // tiles accumulated (1 pass: TMEM buffer = tcount & 1)
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_units && ok; tile += unit_step) {
+      for (int tile = first_unit; tile < total_units && ok; tile += unit_step) {
         const TileInfo t = tile_at(tile);
         if (t.skip) continue;
         const int num_k = t.num_k;
@@ -361,12 +422,12 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
           const bool first_in_chunk = Cfg::kChunked ? (kt % Cfg::kChunk == 0) : (kt == 0);
           const bool last_in_chunk = Cfg::kChunked && (kt % Cfg::kChunk == Cfg::kChunk - 1 || kt == num_k - 1);
           if (Cfg::kChunked && first_in_chunk && chunk >= 2 &&
-              !mbar_wait(&chunk_empty[buf], ((chunk >> 1) - 1) & 1, p.status, kStatusTimeoutAccum)) {
+              !wait_in(&chunk_empty[buf], ((chunk >> 1) - 1) & 1, kStatusTimeoutAccum)) {
             ok = false;
             break;
           }
           uint64_t* ready = PASSES == 3 ? &conv_bar[s] : &full_bar[s];
-          if (!mbar_wait(ready, use & 1, p.status, PASSES == 3 ? kStatusTimeoutConvert : kStatusTimeoutFull)) {
+          if (!wait_in(ready, use & 1, PASSES == 3 ? kStatusTimeoutConvert : kStatusTimeoutFull)) {
             ok = false;
             break;
           }
@@ -386,18 +447,25 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
             };
             const uint32_t acc = (first_in_chunk && ks == 0) ? 0u : 1u;
             if (PASSES == 3) {
-              const uint32_t ta_hi = tmem_base + Cfg::kATmem + s * 2 * BK + ks * 8;
+              const uint32_t ta_hi = tmem_base + Cfg::kATmem + (it % Cfg::kAStages) * 2 * BK + ks * 8;
               const uint32_t ta_lo = ta_hi + BK;
               const uint32_t b_lo = smem_u32(stage_blo(s));
-              mma_tf32_ts(d_tmem, ta_lo, desc_b(b_hi), idesc, acc);
-              mma_tf32_ts(d_tmem, ta_hi, desc_b(b_lo), idesc, 1u);
-              mma_tf32_ts(d_tmem, ta_hi, desc_b(b_hi), idesc, 1u);
+              if constexpr (PAIR) {
+                mma_tf32_ts_pair(d_tmem, ta_lo, desc_b(b_hi), idesc, acc);
+                mma_tf32_ts_pair(d_tmem, ta_hi, desc_b(b_lo), idesc, 1u);
+                mma_tf32_ts_pair(d_tmem, ta_hi, desc_b(b_hi), idesc, 1u);
+              } else {
+                mma_tf32_ts(d_tmem, ta_lo, desc_b(b_hi), idesc, acc);
+                mma_tf32_ts(d_tmem, ta_hi, desc_b(b_lo), idesc, 1u);
+                mma_tf32_ts(d_tmem, ta_hi, desc_b(b_hi), idesc, 1u);
+              }
             } else {
               mma_tf32_ss(d_tmem, desc_a(a_hi), desc_b(b_hi), idesc, acc);
             }
           }
-          mma_commit(&empty_bar[s]);
-          if (last_in_chunk) mma_commit(&chunk_full[buf]);
+          if (PASSES == 3 && Cfg::kAStages < STAGES) commit(&a_empty[it % Cfg::kAStages]);
+          commit(&empty_bar[s]);
+          if (last_in_chunk) commit(&chunk_full[buf]);
           issued_any = true;
         }
         if (!ok) break;
@@ -421,7 +489,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     int chunk0 = 0, tcount = 0;
     bool dead = false;  // a wait ran out: skip all work, keep the named barriers
-    for (int tile = blockIdx.x; tile < total_units; tile += unit_step) {
+    for (int tile = first_unit; tile < total_units; tile += unit_step) {
       const TileInfo t = tile_at(tile);
       if (t.skip) continue;
       const int m0 = t.m0, n0 = t.n0, num_k = t.num_k;
@@ -454,7 +522,12 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
             for (int i = 0; i < 32; ++i) acc[c * 32 + i] += __uint_as_float(v[i]);
           }
           tc_fence_before();
-          mbar_arrive(&chunk_empty[buf]);
+          if constexpr (PAIR) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(leader_addr(&chunk_empty[buf]));
+          } else {
+            mbar_arrive(&chunk_empty[buf]);
+          }
         }
         chunk0 += num_chunks;
       } else {
@@ -662,7 +735,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>((warp % 4) * 32) << 16);
     int it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < total_units && ok; tile += unit_step) {
+    for (int tile = first_unit; tile < total_units && ok; tile += unit_step) {
       const TileInfo t = tile_at(tile);
       if (t.skip) continue;
       for (int kt = 0; kt < t.num_k; ++kt, ++it) {
@@ -700,13 +773,23 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
               }
             }
           }
-          tmem_st32(lane_addr + Cfg::kATmem + s * 2 * BK, hi);
-          tmem_st32(lane_addr + Cfg::kATmem + s * 2 * BK + BK, lo);
+          // The TMEM A stage must have been read by the MMAs of k-tile
+          // it - kAStages (with kAStages == STAGES that is already implied by
+          // the TMA landing, which waited for the same MMAs).
+          const int as = it % Cfg::kAStages;
+          if (Cfg::kAStages < STAGES && it >= Cfg::kAStages &&
+              !mbar_wait_warp(&a_empty[as], ((it / Cfg::kAStages) - 1) & 1, p.status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          tmem_st32(lane_addr + Cfg::kATmem + as * 2 * BK, hi);
+          tmem_st32(lane_addr + Cfg::kATmem + as * 2 * BK + BK, lo);
           // B stays raw in the landing buffer (the MMA truncates it to its tf32
           // hi part); only lo is written.
           const float4* bsrc = reinterpret_cast<const float4*>(stage_b(s));
           float4* bdst = reinterpret_cast<float4*>(stage_blo(s));
-          constexpr int kB4 = BN * BK / 4;
+          constexpr int kB4 = Cfg::kBCols * BK / 4;
     #pragma unroll 4
           for (int i = ct; i < kB4; i += 128) {
             const float4 x = bsrc[i];
@@ -715,17 +798,27 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES>::kThrea
           tmem_st_wait();
           fence_proxy_async_smem();
           tc_fence_before();
-        mbar_arrive(&conv_bar[s]);
+        if constexpr (PAIR) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(leader_addr(&conv_bar[s]));
+        } else {
+          mbar_arrive(&conv_bar[s]);
+        }
       }
     }
   }
 
   // ------------------------------------------------------------ teardown
+  // A pair waits for the whole cluster: the leader's MMAs read this CTA's
+  // shared memory and TMEM until its last commit, which the leader's MMA
+  // warp waited for above.
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    else tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
 

@@ -33,10 +33,12 @@ and the combine is a weighted ``index_add`` in sorted order (deterministic).
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
 from abacus_b200.ops import gemm
+from abacus_b200.ops._ext import ext
 from abacus_b200.parallel import ep_fused, mesh, tp_fused
 from abacus_b200.parallel.expert_parallel import (
     _AllToAll,
@@ -75,6 +77,37 @@ def load_balancing_loss(router_probs: torch.Tensor, expert_indices: torch.Tensor
     return (torch.sum(f_E * p_E) * (coeff * n_experts)).to(dtype=router_probs.dtype)
 
 
+class _RouterLogits(torch.autograd.Function):
+    """``x @ w_DE`` on the router kernels (one read of x; no library GEMM)."""
+
+    @staticmethod
+    def forward(ctx, x2, w):
+        out = torch.empty(x2.shape[0], w.shape[1], device=x2.device, dtype=torch.float32)
+        ext().router_logits(x2, w.contiguous(), out)
+        ctx.save_for_backward(x2, w)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        x2, w = ctx.saved_tensors
+        dx = torch.empty_like(x2)
+        dw = torch.empty_like(w)
+        ext().router_logits_bwd(grad.contiguous(), x2, w.contiguous(), dx, dw)
+        return dx, dw
+
+
+def router_logits(x_BLD: torch.Tensor, w_DE: torch.Tensor) -> torch.Tensor:
+    """Router scores (B, L, E) = x @ w_DE: the router kernels for fp32 CUDA
+    inputs with a power-of-two expert count up to 64, ATen otherwise."""
+    e = w_DE.shape[1]
+    if x_BLD.is_cuda and x_BLD.dtype == torch.float32 and e <= 64 and (e & (e - 1)) == 0:
+        x2 = x_BLD.reshape(-1, x_BLD.shape[-1])
+        if x2.stride(1) != 1:
+            x2 = x2.contiguous()
+        return _RouterLogits.apply(x2, w_DE).view(*x_BLD.shape[:-1], e)
+    return x_BLD @ w_DE
+
+
 class Router(torch.nn.Module):
     def __init__(
         self,
@@ -111,7 +144,7 @@ class Router(torch.nn.Module):
 
     def forward(self, x_BLD: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         w_DE = _SumReplicatedGrads.apply(self.w_DE, self.sync_dim) if self.expert_parallel else self.w_DE
-        logits_BLE = x_BLD @ w_DE
+        logits_BLE = router_logits(x_BLD, w_DE)
         if self.router == "softmax":
             probs_BLE = torch.softmax(logits_BLE, dim=-1)
             indices_BLK = torch.topk(probs_BLE.detach(), self.top_k, dim=-1).indices
@@ -356,7 +389,8 @@ class MoEExpertParallel(torch.nn.Module):
             # expert down-projection's epilogue (NVLink peer memory). With a
             # capacity and every routed token local (EP over DP ranks), the
             # slabs are static and the routing never reaches the host.
-            capacity = self._capacity(local_SD.shape[0]) if self.data_parallel else None
+            static = os.environ.get("ABACUS_EP_STATIC", "1") != "0"
+            capacity = self._capacity(local_SD.shape[0]) if self.data_parallel and static else None
             if capacity is not None:
                 return ep_fused.dispatch_combine_capacity(local_SD, weights_SK, indices_SK, self.w_gate_EDM,
                                                           self.w_up_EDM, self.w_down_EMD, self.n_experts, capacity,

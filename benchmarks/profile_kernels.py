@@ -156,7 +156,9 @@ def main():
     for n in names:
         ms, rate, unit = run(n)
         check_status()
-        print(f"{n:10s} {ms:8.3f} ms  {rate:9.1f} {unit}", flush=True)
+        pairs = ext().gemm_pair_clusters() if n in ("gemm3", "wgrad3") else 0
+        note = f"  ({pairs} CTA pairs)" if pairs else ""
+        print(f"{n:10s} {ms:8.3f} ms  {rate:9.1f} {unit}{note}", flush=True)
 
 
 if __name__ == "__main__":

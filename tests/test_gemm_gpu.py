@@ -51,6 +51,52 @@ def test_gemm_layouts(mode, trans_a, trans_b, shape):
     assert err < tol, f"{mode} {shape} ta={trans_a} tb={trans_b}: rel err {err:.3e} (tol {tol:.3e})"
 
 
+@pytest.mark.parametrize("trans_a,trans_b", list(itertools.product([False, True], repeat=2)))
+@pytest.mark.parametrize("shape", [(256, 128, 64), (384, 200, 96), (1000, 640, 768), (512, 256, 8192)])
+def test_cta_pair_gemm_matches_single_cta(monkeypatch, trans_a, trans_b, shape):
+    """fp32 mode on CTA pairs (one cta_group::2 MMA over 256 rows; a ragged
+    last pair; split-K at K = 8192) against fp64 and against one CTA per tile."""
+    m, n, k = shape
+    torch.manual_seed(11)
+    a = torch.randn(k, m, device="cuda") if trans_a else torch.randn(m, k, device="cuda")
+    b = torch.randn(n, k, device="cuda") if trans_b else torch.randn(k, n, device="cuda")
+    outs = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("ABACUS_GEMM_PAIR", flag)
+        outs[flag] = gemm.matmul(a, b, trans_a=trans_a, trans_b=trans_b)
+        torch.cuda.synchronize()
+        check_status()
+    ref = _ref(a, b, trans_a, trans_b)
+    assert _rel_err(outs["1"], ref) < 2e-6
+    assert _rel_err(outs["1"], outs["0"].double()) < 1e-6
+
+
+@pytest.mark.parametrize("tokens", [256, 300, 1024])
+def test_cta_pair_swiglu_matches_single_cta(monkeypatch, tokens):
+    torch.manual_seed(12)
+    dim, hidden = 256, 512
+    x = torch.randn(tokens, dim, device="cuda")
+    wg = torch.randn(dim, hidden, device="cuda") / dim**0.5
+    wu = torch.randn(dim, hidden, device="cuda") / dim**0.5
+    wd = torch.randn(hidden, dim, device="cuda") / hidden**0.5
+    gy = torch.randn(tokens, dim, device="cuda")
+    res = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("ABACUS_GEMM_PAIR", flag)
+        leaves = [t.clone().requires_grad_() for t in (x, wg, wu, wd)]
+        y = gemm.swiglu_mlp(*leaves)
+        y.backward(gy)
+        torch.cuda.synchronize()
+        check_status()
+        res[flag] = [y.detach()] + [t.grad for t in leaves]
+    xd, wgd, wud, wdd = [t.double().requires_grad_() for t in (x, wg, wu, wd)]
+    yd = (torch.nn.functional.silu(xd @ wgd) * (xd @ wud)) @ wdd
+    yd.backward(gy.double())
+    for got, single, ref in zip(res["1"], res["0"], [yd.detach(), xd.grad, wgd.grad, wud.grad, wdd.grad]):
+        assert _rel_err(got, ref) < 1e-5
+        assert _rel_err(got, single.double()) < 1e-6
+
+
 def test_fp32_mode_matches_sgemm_accuracy():
     torch.manual_seed(1)
     a = torch.randn(512, 768, device="cuda")

@@ -150,3 +150,26 @@ def test_transpose_kernel(rows, cols):
     assert torch.equal(gemm.transpose(x), x.t())
     view = torch.randn(rows, cols + 3, device="cuda")[:, 1 : cols + 1]  # unaligned, strided rows
     assert torch.equal(gemm.transpose(view), view.t())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tokens,dim,experts", [(4096, 768, 8), (333, 256, 2), (64, 128, 64)])
+def test_router_logits_kernels_match_fp64(tokens, dim, experts):
+    from abacus_b200.models.moe import router_logits
+
+    g = torch.Generator(device="cuda").manual_seed(tokens)
+    x = torch.randn(2, tokens // 2 + tokens % 2, dim, device="cuda", generator=g)[:, : tokens // 2]
+    w = torch.randn(dim, experts, device="cuda", generator=g) / dim**0.5
+    x.requires_grad_(True)
+    w.requires_grad_(True)
+    out = router_logits(x, w)
+    gout = torch.randn_like(out)
+    out.backward(gout)
+    xd, wd = x.detach().double().requires_grad_(True), w.detach().double().requires_grad_(True)
+    ref = xd @ wd
+    ref.backward(gout.double())
+    rel = lambda a, b: ((a.double() - b).abs().max() / b.abs().max()).item()  # noqa: E731
+    assert rel(out, ref) < 1e-5
+    assert rel(x.grad, xd.grad) < 1e-5
+    assert rel(w.grad, wd.grad) < 1e-5
+    check_status()

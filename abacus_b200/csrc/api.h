@@ -9,6 +9,13 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
               int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate, int64_t passes);
 int64_t gemm_n_tiles(int64_t n, int64_t passes);
 int64_t gemm_pair_clusters();
+int64_t gemm_grouped(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
+                     int64_t b_mode, double alpha, bool accumulate, int64_t passes,
+                     c10::optional<std::vector<int64_t>> scatter);
+void gemm_swiglu_grouped(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
+                         torch::Tensor h, int64_t passes, c10::optional<std::vector<int64_t>> wait);
+void gemm_swiglu_bwd_grouped(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u,
+                             torch::Tensor dgu, int64_t passes, c10::optional<std::vector<int64_t>> wait);
 int64_t gemm_out_tp(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
                     int64_t b_mode, double alpha, int64_t passes, c10::optional<std::vector<int64_t>> wait,
                     c10::optional<std::vector<int64_t>> scatter);

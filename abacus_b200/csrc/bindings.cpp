@@ -9,6 +9,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_out", &abacus::gemm::gemm_out, "tcgen05 tf32 / 3xTF32 GEMM into C");
   m.def("gemm_n_tiles", &abacus::gemm::gemm_n_tiles, "N tiles of a single-B GEMM of the given output width");
   m.def("gemm_pair_clusters", &abacus::gemm::gemm_pair_clusters, "CTA pairs of the last CTA-pair GEMM launch");
+  m.def("gemm_grouped", &abacus::gemm::gemm_grouped, "one GEMM launch over (experts, rows, cols) operands");
+  m.def("gemm_swiglu_grouped", &abacus::gemm::gemm_swiglu_grouped, "grouped gate/up GEMM with SwiGLU epilogue");
+  m.def("gemm_swiglu_bwd_grouped", &abacus::gemm::gemm_swiglu_bwd_grouped,
+        "grouped down-projection dgrad with SwiGLU backward epilogue");
   m.def("gemm_out_tp", &abacus::gemm::gemm_out_tp, "GEMM with a peer-gathered operand and/or row-scattered output");
   m.def("gemm_swiglu_tp", &abacus::gemm::gemm_swiglu_tp, "SwiGLU up-projection over a peer-gathered input");
   m.def("gemm_swiglu_bwd_tp", &abacus::gemm::gemm_swiglu_bwd_tp, "SwiGLU backward GEMM over a peer-gathered dy");

@@ -434,6 +434,199 @@ void gemm_batched(torch::Tensor c, torch::Tensor a, torch::Tensor b, bool trans_
                static_cast<int>(passes), at::cuda::getCurrentCUDAStream());
 }
 
+// ------------------------------------------------------------ grouped GEMMs
+// One launch over E experts: every operand is a 3-D (E, rows, cols) view
+// (expert e's matrix at index e), mapped as a 4-D (1, E, rows, cols) TMA
+// tensor; the tile schedule walks (tile, expert) units. Epilogue tensors that
+// are indexed by row (SwiGLU outputs, the row-map scatter meta) stack the
+// experts' rows: expert e's row r is row e * rows + r.
+namespace {
+
+torch::Tensor as4(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 3, name, " must be a 3-D (experts, rows, cols) view");
+  return t.unsqueeze(0);
+}
+
+// Rows of a stacked 3-D view (stride(0) == rows * stride(1)), for the
+// row-indexed epilogue tensors.
+void check_stacked(const torch::Tensor& t, int64_t rows, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32 && t.dim() == 3 && t.stride(2) == 1, name,
+              " must be a 3-D CUDA fp32 view with unit inner stride");
+  TORCH_CHECK(t.size(1) == rows && t.stride(0) == rows * t.stride(1), name, " must stack ", rows, " rows per expert");
+}
+
+}  // namespace
+
+// C[e] = alpha * op(A[e]) @ op(B[e]) (+ C[e]) for every expert e, one launch.
+// b_mode 0 (single) or 2 (K-segmented: A's columns are the concatenation of
+// the segments' K ranges). scatter: row-map mode only ([-1, meta, bases...,
+// counters...]; meta indexed by stacked output row), C then only fixes the row
+// stride.
+int64_t gemm_grouped(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
+                     int64_t b_mode, double alpha, bool accumulate, int64_t passes,
+                     c10::optional<std::vector<int64_t>> scatter) {
+  check_passes(passes);
+  TORCH_CHECK(!bs.empty() && bs.size() <= 3, "between 1 and 3 B operands");
+  TORCH_CHECK(b_mode == kBSingle || b_mode == kBSegK, "grouped GEMMs take a single or K-segmented B");
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto a4 = as4(a, "A");
+  check_batched(a4, "A");
+  std::vector<torch::Tensor> b4;
+  for (auto& b : bs) {
+    b4.push_back(as4(b, "B"));
+    check_batched(b4.back(), "B");
+    TORCH_CHECK(b.size(0) == a.size(0), "every operand needs one matrix per expert");
+  }
+  const int64_t E = a.size(0);
+  const bool a_mn = trans_a, b_mn = !trans_b;
+  const int64_t M = a_mn ? a.size(2) : a.size(1), K = a_mn ? a.size(1) : a.size(2);
+  const int64_t N = b_mn ? bs[0].size(2) : bs[0].size(1);
+  const int64_t seg = b_mn ? bs[0].size(1) : bs[0].size(2);
+  for (auto& b : bs) TORCH_CHECK((b_mn ? b.size(2) : b.size(1)) == N && (b_mn ? b.size(1) : b.size(2)) == seg, "B shapes differ");
+  if (b_mode == kBSingle) {
+    TORCH_CHECK(bs.size() == 1 && seg == K, "inner dimensions differ: ", K, " vs ", seg);
+  } else {
+    TORCH_CHECK(seg % BK == 0 && K == seg * static_cast<int64_t>(bs.size()), "K segments must be whole k-tiles summing to K");
+  }
+  const Comm cm = make_comm(c10::nullopt, scatter);
+  const bool scattered = !cm.scatter.empty();
+  TORCH_CHECK(!scattered || cm.scatter[0] == -1, "grouped GEMMs scatter by row map only");
+  TORCH_CHECK(!scattered || !accumulate, "scatter GEMMs do not accumulate");
+  auto c4 = as4(c, "C");
+  if (!scattered) {
+    check_batched(c4, "C");
+    TORCH_CHECK(c.size(0) == E && c.size(1) == M && c.size(2) == N, "C shape mismatch");
+  } else {
+    TORCH_CHECK(c.stride(2) == 1 && c.size(2) == N && c.stride(1) == N, "scatter staging rows must be (.., N) contiguous");
+  }
+  if (M == 0 || N == 0 || E == 0) return 0;
+  TORCH_CHECK(K > 0, "empty inner dimension");
+  TORCH_CHECK(E <= 65535, "at most 65535 experts per grouped GEMM");
+  const int BN = pick_bn(N, static_cast<int>(passes));
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.tma_a = a_mn ? make_map4(a4, 32, BK, true) : make_map4(a4, BK, BM, false);
+  for (size_t i = 0; i < b4.size(); ++i) p.tma_b[i] = b_mn ? make_map4(b4[i], 32, BK, true) : make_map4(b4[i], BK, BN, false);
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.b_mode = static_cast<int>(b_mode);
+  p.seg = static_cast<int>(seg);
+  p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
+  p.alpha = static_cast<float>(alpha);
+  p.accumulate = accumulate ? 1 : 0;
+  p.c = c.data_ptr<float>();
+  p.ldc = c.stride(1);
+  p.batched = 1;
+  p.batch_h = static_cast<int>(E);
+  p.c_stride_h = c.stride(0);
+  p.z_rows = M;
+  p.status = host::status_ptr(a.device().index());
+  apply_comm(p, cm, a_mn, b_mn);
+  p.k_tiles_per_split = static_cast<int>((K + BK - 1) / BK);
+  const long long tiles = ((M + BM - 1) / BM) * p.num_n_tiles;
+  p.splits = 1;
+  p.batch_z = static_cast<int>(E);
+  const unsigned grid = tile_grid(p, tiles * E, a.device().index());
+  launch_store(p, dim3(grid, 1, 1), BN, a_mn, b_mn, static_cast<int>(passes), at::cuda::getCurrentCUDAStream());
+  return scattered ? p.num_n_tiles : 0;
+}
+
+// Grouped SwiGLU up-projection: for every expert e, g[e] = x[e] @ w_gate[e],
+// u[e] = x[e] @ w_up[e], h[e] = silu(g[e]) * u[e]. x (E, C, D); w (E, D, Mh);
+// g / u / h (E, C, Mh) stacked. wait: as gemm_swiglu_tp (x rows pushed by peers).
+void gemm_swiglu_grouped(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
+                         torch::Tensor h, int64_t passes, c10::optional<std::vector<int64_t>> wait) {
+  check_passes(passes);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto x4 = as4(x, "x"), wg4 = as4(w_gate, "w_gate"), wu4 = as4(w_up, "w_up");
+  check_batched(x4, "x");
+  check_batched(wg4, "w_gate");
+  check_batched(wu4, "w_up");
+  const int64_t E = x.size(0), C = x.size(1), D = x.size(2), Mh = w_gate.size(2);
+  TORCH_CHECK(w_gate.size(0) == E && w_up.size(0) == E && w_gate.size(1) == D && w_up.sizes() == w_gate.sizes(),
+              "grouped SwiGLU weight shapes");
+  for (auto* t : {&g, &u, &h}) check_stacked(*t, C, "SwiGLU output");
+  TORCH_CHECK(g.stride(1) == h.stride(1) && u.stride(1) == h.stride(1) && g.size(2) == Mh && u.size(2) == Mh &&
+                  h.size(2) == Mh && g.size(0) == E,
+              "SwiGLU outputs must share (E, C, hidden) shape and row stride");
+  if (E == 0 || C == 0 || Mh == 0) return;
+  const int BN = passes == 3 ? 128 : 256;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.tma_a = make_map4(x4, BK, BM, false);
+  p.tma_b[0] = make_map4(wg4, 32, BK, true);
+  p.tma_b[1] = make_map4(wu4, 32, BK, true);
+  p.M = static_cast<int>(C);
+  p.N = static_cast<int>(Mh);
+  p.K = static_cast<int>(D);
+  p.b_mode = kBDualN;
+  p.num_n_tiles = static_cast<int>((Mh + BN / 2 - 1) / (BN / 2));
+  p.alpha = 1.f;
+  p.g = g.data_ptr<float>();
+  p.u = u.data_ptr<float>();
+  p.h = h.data_ptr<float>();
+  p.ldh = h.stride(1);
+  p.batched = 1;
+  p.batch_h = static_cast<int>(E);
+  p.z_rows = C;
+  p.status = host::status_ptr(x.device().index());
+  apply_comm(p, make_comm(wait, c10::nullopt), false, true);
+  p.k_tiles_per_split = static_cast<int>((D + BK - 1) / BK);
+  const long long tiles = ((C + BM - 1) / BM) * p.num_n_tiles;
+  p.splits = 1;
+  p.batch_z = static_cast<int>(E);
+  const unsigned grid = tile_grid(p, tiles * E, x.device().index());
+  launch_swiglu(p, dim3(grid, 1), BN, static_cast<int>(passes), at::cuda::getCurrentCUDAStream());
+}
+
+// Grouped SwiGLU backward through the hidden layer: dh[e] = dy[e] @ w_down[e]^T,
+// dgu[e] = [dh * u * silu'(g) | dh * silu(g)]. dy (E, C, D); w_down (E, Mh, D);
+// g / u (E, C, Mh) and dgu (E, C, 2 Mh) stacked.
+void gemm_swiglu_bwd_grouped(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u,
+                             torch::Tensor dgu, int64_t passes, c10::optional<std::vector<int64_t>> wait) {
+  check_passes(passes);
+  const c10::cuda::CUDAGuard guard(dy.device());
+  auto dy4 = as4(dy, "dy"), wd4 = as4(w_down, "w_down");
+  check_batched(dy4, "dy");
+  check_batched(wd4, "w_down");
+  const int64_t E = dy.size(0), C = dy.size(1), D = dy.size(2), Mh = w_down.size(1);
+  TORCH_CHECK(w_down.size(0) == E && w_down.size(2) == D, "w_down shape");
+  check_stacked(g, C, "g");
+  check_stacked(u, C, "u");
+  check_stacked(dgu, C, "dgu");
+  TORCH_CHECK(g.size(2) == Mh && u.sizes() == g.sizes() && u.stride(1) == g.stride(1) && dgu.size(2) == 2 * Mh,
+              "g / u (E, C, hidden), dgu (E, C, 2 hidden)");
+  if (E == 0 || C == 0 || Mh == 0) return;
+  const int BN = passes == 3 ? 128 : (Mh >= 2048 ? 256 : 128);
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.tma_a = make_map4(dy4, BK, BM, false);
+  p.tma_b[0] = make_map4(wd4, BK, BN, false);
+  p.M = static_cast<int>(C);
+  p.N = static_cast<int>(Mh);
+  p.K = static_cast<int>(D);
+  p.b_mode = kBSingle;
+  p.num_n_tiles = static_cast<int>((Mh + BN - 1) / BN);
+  p.alpha = 1.f;
+  p.g_in = g.data_ptr<float>();
+  p.u_in = u.data_ptr<float>();
+  p.ld_gu = g.stride(1);
+  p.dgu = dgu.data_ptr<float>();
+  p.ld_dgu = dgu.stride(1);
+  p.batched = 1;
+  p.batch_h = static_cast<int>(E);
+  p.z_rows = C;
+  p.status = host::status_ptr(dy.device().index());
+  apply_comm(p, make_comm(wait, c10::nullopt), false, false);
+  p.k_tiles_per_split = static_cast<int>((D + BK - 1) / BK);
+  const long long tiles = ((C + BM - 1) / BM) * p.num_n_tiles;
+  p.splits = 1;
+  p.batch_z = static_cast<int>(E);
+  const unsigned grid = tile_grid(p, tiles * E, dy.device().index());
+  launch_swiglu_bwd(p, dim3(grid, 1), BN, static_cast<int>(passes), at::cuda::getCurrentCUDAStream());
+}
+
 // SwiGLU up-projection: g = x @ w_gate, u = x @ w_up, h = silu(g) * u.
 // x (T, D), w_gate / w_up (D, Mh) in the (in, out) layout.
 void gemm_swiglu(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,

@@ -65,6 +65,10 @@ struct alignas(64) Params {
   int batched;
   int batch_h;
   long long c_stride_h, c_stride_b;
+  // Grouped mode (batched with one matrix per expert, H = experts): the
+  // row-indexed epilogue tensors (SwiGLU g / u / h, g_in / u_in / dgu, and the
+  // row-map scatter meta) stack the experts' rows, z_rows rows per expert.
+  long long z_rows;
   // Causal structure of attention-shaped products (square, queries = keys):
   //   1: skip tiles strictly above the diagonal (n0 >= m0 + BM), C untouched
   //   2: K range [0, m0 + BM)   (P @ V, dS @ K: keys after the last query)
@@ -494,6 +498,8 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
       if (t.skip) continue;
       const int m0 = t.m0, n0 = t.n0, num_k = t.num_k;
       const int row = m0 + q * 32 + lane;
+      // Row of the stacked (grouped) epilogue tensors.
+      const long long grow = row + static_cast<long long>(t.zh) * p.z_rows;
       bool ok = num_k > 0 && !dead;
       const int abuf = tcount & 1;
       // fp32 (3xTF32) mode: drain each K-chunk accumulator into registers with
@@ -561,10 +567,10 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
           const int col0 = n0 + c * 32;
           // Row-map scatter: rows whose meta is negative (unfilled capacity
           // slots of an expert slab) are computed but not returned.
-          if (row_ok && col0 < p.N && (!p.scatter_meta || p.scatter_meta[row] >= 0)) {
+          if (row_ok && col0 < p.N && (!p.scatter_meta || p.scatter_meta[grow] >= 0)) {
             float* crow;
             if (p.scatter_meta) {
-              const int meta = p.scatter_meta[row];
+              const int meta = p.scatter_meta[grow];
               crow = p.scatter_base[meta & 7] + static_cast<long long>(meta >> 3) * p.ldc + col0;
             } else if (p.scatter_chunk) {
               const int pos = row % p.scatter_seq;
@@ -612,7 +618,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
           group(c + BN / 64, uv);
           const int col0 = n0 + c * 32;
           if (row_ok && col0 < p.N) {
-            const long long off = static_cast<long long>(row) * p.ldh + col0;
+            const long long off = grow * p.ldh + col0;
             const bool vec = col0 + 32 <= p.N && (p.ldh & 3) == 0 &&
                              ((reinterpret_cast<uintptr_t>(p.g) | reinterpret_cast<uintptr_t>(p.u) |
                                reinterpret_cast<uintptr_t>(p.h)) & 15) == 0;
@@ -645,8 +651,8 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
           group(c, v);
           const int col0 = n0 + c * 32;
           if (row_ok && col0 < p.N) {
-            const long long off = static_cast<long long>(row) * p.ld_gu + col0;
-            const long long doff = static_cast<long long>(row) * p.ld_dgu + col0;
+            const long long off = grow * p.ld_gu + col0;
+            const long long doff = grow * p.ld_dgu + col0;
             const bool vec = col0 + 32 <= p.N && ((p.ld_gu | p.ld_dgu | p.N) & 3) == 0 &&
                              ((reinterpret_cast<uintptr_t>(p.g_in) | reinterpret_cast<uintptr_t>(p.u_in) |
                                reinterpret_cast<uintptr_t>(p.dgu)) & 15) == 0;
@@ -710,7 +716,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
         __threadfence_system();
         if (lane == 0) epi_ok[q] = ok ? 1 : 0;
         named_barrier_sync(1, 128);
-        const int meta_row = row_ok ? p.scatter_meta[row] : -1;
+        const int meta_row = row_ok ? p.scatter_meta[grow] : -1;
         const int dest = meta_row >= 0 ? (meta_row & 7) : -1;
   #pragma unroll
         for (int d = 0; d < 8; ++d) {

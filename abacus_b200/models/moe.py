@@ -26,9 +26,12 @@ Options beyond the reference (defaults reproduce it):
   replicated batch; no gather-v is needed and non-expert gradients are
   averaged by the data-parallel wrapper.
 
-The expert loop runs as grouped work: tokens are permuted by expert with one
-stable sort, each expert's contiguous slab runs the fused SwiGLU GEMM path,
-and the combine is a weighted ``index_add`` in sorted order (deterministic).
+Without a capacity factor, tokens are permuted by expert with one stable
+sort, each expert's contiguous slab runs the fused SwiGLU GEMM path, and the
+combine is a weighted ``index_add`` in sorted order (deterministic). With a
+capacity factor (CUDA), every expert owns a static slab of C rows and all
+experts run as one grouped launch per product (``gemm.grouped_swiglu_mlp``),
+with no host sync.
 """
 from __future__ import annotations
 
@@ -224,9 +227,9 @@ def _grouped_experts_capacity(x_TD, weights_TK, indices_TK, w_gate_EDM, w_up_EDM
     slot = torch.where(keep, flat_e * capacity + within, spill)
     token_of = torch.arange(t, device=x_TD.device).repeat_interleave(k)
     slab = x_TD.new_zeros(spill + 1, x_TD.shape[1]).index_copy(0, slot, x_TD.index_select(0, token_of))
-    outs = [_expert_forward(slab[e * capacity : (e + 1) * capacity], w_gate_EDM[e], w_up_EDM[e], w_down_EMD[e])
-            for e in range(n_experts)]
-    y_slab = torch.cat(outs + [x_TD.new_zeros(1, x_TD.shape[1])], dim=0)
+    # All experts in one grouped launch per product (every slab has C rows).
+    y_ECD = gemm.grouped_swiglu_mlp(slab[:spill].view(n_experts, capacity, -1), w_gate_EDM, w_up_EDM, w_down_EMD)
+    y_slab = torch.cat((y_ECD.reshape(spill, -1), x_TD.new_zeros(1, x_TD.shape[1])), dim=0)
     y_TKD = y_slab.index_select(0, slot).view(t, k, -1)
     return (y_TKD * (weights_TK * keep.view(t, k)).unsqueeze(-1)).sum(dim=1)
 

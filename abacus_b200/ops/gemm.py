@@ -185,6 +185,58 @@ def swiglu_mlp(
     return _SwiGLU.apply(x.contiguous(), w_gate, w_up, w_down, residual)
 
 
+class _GroupedSwiGLU(torch.autograd.Function):
+    """``_SwiGLU`` for E experts at once: x (E, C, D) holds every expert's C
+    rows, w_gate / w_up (E, D, Mh), w_down (E, Mh, D). Each product is one
+    grouped launch over all experts (``gemm_grouped`` / ``gemm_swiglu_grouped``),
+    so the expert loop costs 2 forward and 6 backward launches for any E.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w_gate, w_up, w_down):
+        n_exp, rows, _ = x.shape
+        hidden = w_gate.shape[2]
+        passes = precision.passes()
+        g = torch.empty(n_exp, rows, hidden, device=x.device, dtype=torch.float32)
+        u = torch.empty_like(g)
+        h = torch.empty_like(g)
+        ext().gemm_swiglu_grouped(x, w_gate, w_up, g, u, h, passes, None)
+        y = torch.empty(n_exp, rows, w_down.shape[2], device=x.device, dtype=torch.float32)
+        ext().gemm_grouped(y, h, [w_down], False, False, B_SINGLE, 1.0, False, passes, None)
+        ctx.save_for_backward(x, w_gate, w_up, w_down, g, u, h)
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_y):
+        x, w_gate, w_up, w_down, g, u, h = ctx.saved_tensors
+        gy = grad_y.contiguous()
+        n_exp, rows, _ = x.shape
+        hidden = w_gate.shape[2]
+        passes = precision.passes()
+        dgu = torch.empty(n_exp, rows, 2 * hidden, device=gy.device, dtype=torch.float32)
+        ext().gemm_swiglu_bwd_grouped(gy, w_down, g, u, dgu, passes, None)
+        dx = torch.empty_like(x)
+        if hidden % 32 == 0:
+            ext().gemm_grouped(dx, dgu, [w_gate, w_up], False, True, B_SEG_K, 1.0, False, passes, None)
+        else:  # K segments must be whole 32-element k-tiles: two accumulating GEMMs
+            ext().gemm_grouped(dx, dgu[..., :hidden], [w_gate], False, True, B_SINGLE, 1.0, False, passes, None)
+            ext().gemm_grouped(dx, dgu[..., hidden:], [w_up], False, True, B_SINGLE, 1.0, True, passes, None)
+        d_gate = torch.empty_like(w_gate)
+        d_up = torch.empty_like(w_up)
+        d_down = torch.empty_like(w_down)
+        ext().gemm_grouped(d_gate, x, [dgu[..., :hidden]], True, False, B_SINGLE, 1.0, False, passes, None)
+        ext().gemm_grouped(d_up, x, [dgu[..., hidden:]], True, False, B_SINGLE, 1.0, False, passes, None)
+        ext().gemm_grouped(d_down, h, [gy], True, False, B_SINGLE, 1.0, False, passes, None)
+        return dx, d_gate, d_up, d_down
+
+
+def grouped_swiglu_mlp(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    """Per-expert SwiGLU MLP over (E, C, D) rows: y[e] = (silu(x[e] Wg[e]) * (x[e] Wu[e])) Wd[e]."""
+    if not x.is_cuda:
+        return torch.bmm(torch.nn.functional.silu(torch.bmm(x, w_gate)) * torch.bmm(x, w_up), w_down)
+    return _GroupedSwiGLU.apply(x.contiguous(), w_gate.contiguous(), w_up.contiguous(), w_down.contiguous())
+
+
 class _QKVProjection(torch.autograd.Function):
     """``[x @ Wq | x @ Wk | x @ Wv]`` as one N-segmented GEMM (T, 3*HK).
 

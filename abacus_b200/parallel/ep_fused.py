@@ -268,18 +268,17 @@ class _EPFusedCapacity(torch.autograd.Function):
         xs_all, meta, wait = _static_push(ws, call + ".X", x.contiguous(), top_k, dest_rank, dest_row, None, rows, dim)
         ret, ret_ptrs, counter_ptrs, counter = _return_target(ws, call + ".R", n * top_k, dim)
         n_tiles = ext().gemm_n_tiles(dim, passes)
-        saved = []
-        for le in range(local_experts):
-            xs = xs_all[le * slab_rows : (le + 1) * slab_rows]
-            g = torch.empty(slab_rows, hidden, device=x.device, dtype=torch.float32)
-            u = torch.empty_like(g)
-            h = torch.empty_like(g)
-            ext().gemm_swiglu_tp(xs, w_gate[le], w_up[le], g, u, h, passes, wait)
-            mrow = meta[le * slab_rows : (le + 1) * slab_rows]
-            scatter = [-1, mrow.data_ptr()] + list(ret_ptrs) + list(counter_ptrs)
-            ext().gemm_out_tp(ret[:dim].view(1, dim), h, [w_down[le]], False, False, _SINGLE, 1.0, passes, None,
-                              scatter)
-            saved.append((g, u, h))
+        # All local experts in one grouped launch per product: the up-projection
+        # waits for every rank's pushed rows, the down-projection's epilogue
+        # returns each row to its source rank (row map = meta, stacked rows).
+        xs3 = xs_all.view(local_experts, slab_rows, dim)
+        g = torch.empty(local_experts, slab_rows, hidden, device=x.device, dtype=torch.float32)
+        u = torch.empty_like(g)
+        h = torch.empty_like(g)
+        ext().gemm_swiglu_grouped(xs3, w_gate, w_up, g, u, h, passes, wait)
+        scatter = [-1, meta.data_ptr()] + list(ret_ptrs) + list(counter_ptrs)
+        ext().gemm_grouped(ret[:dim].view(1, 1, dim), h, [w_down], False, False, _SINGLE, 1.0, False, passes, scatter)
+        saved = (g, u, h)
         ext().ep_credit(counter, dropped, n_tiles)
         target = ws.add_target(call + ".R", n * top_k * n_tiles)
         out = torch.empty(n, dim, device=x.device, dtype=torch.float32)
@@ -309,20 +308,19 @@ class _EPFusedCapacity(torch.autograd.Function):
         d_gate = torch.empty_like(w_gate)
         d_up = torch.empty_like(w_up)
         d_down = torch.empty_like(w_down)
-        for le, (g, u, h) in enumerate(ctx.saved):
-            lo, hi = le * slab_rows, (le + 1) * slab_rows
-            dys = dy_all[lo:hi]
-            dgu = torch.empty(slab_rows, 2 * hidden, device=grad_out.device, dtype=torch.float32)
-            ext().gemm_swiglu_bwd_tp(dys, w_down[le], g, u, dgu, passes, wait)
-            scatter = [-1, meta[lo:hi].data_ptr()] + list(dret_ptrs) + list(counter_ptrs)
-            ext().gemm_out_tp(dret[:dim].view(1, dim), dgu, [w_gate[le], w_up[le]], False, True, _SEG_K, 1.0,
-                              passes, None, scatter)
-            xs = xs_all[lo:hi]
-            # Unfilled slab rows hold zero gradients (their dY rows are zero),
-            # so they add nothing to the weight gradients.
-            ext().gemm_out(d_gate[le], xs, [dgu[:, :hidden]], True, False, _SINGLE, 1.0, None, False, passes)
-            ext().gemm_out(d_up[le], xs, [dgu[:, hidden:]], True, False, _SINGLE, 1.0, None, False, passes)
-            ext().gemm_out(d_down[le], h, [dys], True, False, _SINGLE, 1.0, None, False, passes)
+        g, u, h = ctx.saved
+        dys3 = dy_all.view(local_experts, slab_rows, dim)
+        xs3 = xs_all.view(local_experts, slab_rows, dim)
+        dgu = torch.empty(local_experts, slab_rows, 2 * hidden, device=grad_out.device, dtype=torch.float32)
+        ext().gemm_swiglu_bwd_grouped(dys3, w_down, g, u, dgu, passes, wait)
+        scatter = [-1, meta.data_ptr()] + list(dret_ptrs) + list(counter_ptrs)
+        ext().gemm_grouped(dret[:dim].view(1, 1, dim), dgu, [w_gate, w_up], False, True, _SEG_K, 1.0, False, passes,
+                           scatter)
+        # Unfilled slab rows hold zero gradients (their dY rows are zero), so
+        # they add nothing to the weight gradients.
+        ext().gemm_grouped(d_gate, xs3, [dgu[..., :hidden]], True, False, _SINGLE, 1.0, False, passes, None)
+        ext().gemm_grouped(d_up, xs3, [dgu[..., hidden:]], True, False, _SINGLE, 1.0, False, passes, None)
+        ext().gemm_grouped(d_down, h, [dys3], True, False, _SINGLE, 1.0, False, passes, None)
         dx_tiles = ext().gemm_n_tiles(dim, passes)
         ext().ep_credit(counter, dropped, dx_tiles)
         target = ws.add_target(call + ".dR", n * top_k * dx_tiles)

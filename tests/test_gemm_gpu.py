@@ -218,3 +218,50 @@ def test_batched_gemm_strided_heads(mode, trans_a, trans_b):
     ref = 0.5 * aa @ bm
     err = ((c.double() - ref).abs().max() / ref.abs().max()).item()
     assert err < (3e-3 if mode == "tf32" else 2e-6)
+
+
+@pytest.mark.parametrize("trans_a,trans_b", list(itertools.product([False, True], repeat=2)))
+@pytest.mark.parametrize("experts,m,n,k", [(3, 200, 136, 72), (4, 256, 384, 512), (2, 132, 128, 1024)])
+def test_grouped_gemm_matches_per_expert(trans_a, trans_b, experts, m, n, k):
+    """One launch over E experts (3-D operands) against fp64 per expert."""
+    from abacus_b200.ops._ext import ext
+
+    torch.manual_seed(13)
+    a = torch.randn(experts, k, m, device="cuda") if trans_a else torch.randn(experts, m, k, device="cuda")
+    b = torch.randn(experts, n, k, device="cuda") if trans_b else torch.randn(experts, k, n, device="cuda")
+    c = torch.empty(experts, m, n, device="cuda")
+    ext().gemm_grouped(c, a, [b], trans_a, trans_b, gemm.B_SINGLE, 1.0, False, precision.passes(), None)
+    torch.cuda.synchronize()
+    check_status()
+    ref = torch.stack([_ref(a[e], b[e], trans_a, trans_b) for e in range(experts)])
+    assert _rel_err(c, ref) < 2e-6
+    # accumulate and K segments
+    c2 = torch.randn(experts, m, n, device="cuda")
+    base = c2.double()
+    if not trans_a and trans_b and k % 64 == 0:
+        halves = [b[..., : k // 2].contiguous(), b[..., k // 2 :].contiguous()]
+        ext().gemm_grouped(c2, a, halves, False, True, gemm.B_SEG_K, 0.5, True, precision.passes(), None)
+        torch.cuda.synchronize()
+        check_status()
+        assert _rel_err(c2, base + 0.5 * ref) < 2e-6
+
+
+@pytest.mark.parametrize("experts,rows,dim,hidden", [(4, 160, 128, 256), (3, 300, 256, 688), (8, 512, 768, 1536)])
+def test_grouped_swiglu_matches_fp64(experts, rows, dim, hidden):
+    torch.manual_seed(14)
+    x = torch.randn(experts, rows, dim, device="cuda", requires_grad=True)
+    wg = (torch.randn(experts, dim, hidden, device="cuda") / dim**0.5).requires_grad_()
+    wu = (torch.randn(experts, dim, hidden, device="cuda") / dim**0.5).requires_grad_()
+    wd = (torch.randn(experts, hidden, dim, device="cuda") / hidden**0.5).requires_grad_()
+    y = gemm.grouped_swiglu_mlp(x, wg, wu, wd)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    torch.cuda.synchronize()
+    check_status()
+    leaves = [x, wg, wu, wd]
+    xd, wgd, wud, wdd = [t.detach().double().requires_grad_() for t in leaves]
+    yd = torch.bmm(torch.nn.functional.silu(torch.bmm(xd, wgd)) * torch.bmm(xd, wud), wdd)
+    yd.backward(gy.double())
+    assert _rel_err(y, yd.detach()) < 1e-5
+    for got, ref in zip([t.grad for t in leaves], [xd.grad, wgd.grad, wud.grad, wdd.grad]):
+        assert _rel_err(got, ref) < 1e-5

@@ -9,6 +9,7 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
               int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate, int64_t passes);
 int64_t gemm_n_tiles(int64_t n, int64_t passes);
 int64_t gemm_pair_clusters();
+void gemm_trace(c10::optional<torch::Tensor> buf);
 int64_t gemm_grouped(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
                      int64_t b_mode, double alpha, bool accumulate, int64_t passes,
                      c10::optional<std::vector<int64_t>> scatter);

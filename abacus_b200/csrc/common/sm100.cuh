@@ -437,5 +437,8 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // lo = tf32(x - tf32_trunc(x)) must be written beside it.
 __device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
 __device__ __forceinline__ float tf32_lo_of_raw(float x) { return to_tf32(x - tf32_trunc(x)); }
+// The same with the rounding on the integer ALUs (keeps the conversion unit,
+// which the GEMM converter also needs for every A element, free).
+__device__ __forceinline__ float tf32_lo_of_raw_alu(float x) { return to_tf32_lo(x - tf32_trunc(x)); }
 
 }  // namespace abacus

@@ -222,6 +222,18 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
 
 int64_t gemm_pair_clusters() { return last_pair_clusters(); }
 
+// Phase trace of the following GEMM launches into buf (int64, >= 4096
+// entries, see Params::trace); None turns it off.
+void gemm_trace(c10::optional<torch::Tensor> buf) {
+  if (!buf) {
+    gemm_trace_buffer() = nullptr;
+    return;
+  }
+  TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == torch::kInt64 && buf->is_contiguous() && buf->numel() >= 4096,
+              "trace buffer: contiguous CUDA int64 with at least 4096 entries");
+  gemm_trace_buffer() = reinterpret_cast<long long*>(buf->data_ptr<int64_t>());
+}
+
 // Number of N tiles a single-B GEMM of output width n uses (stores per row).
 int64_t gemm_n_tiles(int64_t n, int64_t passes) {
   check_passes(passes);

@@ -10,6 +10,12 @@
 namespace abacus {
 namespace gemm {
 
+// Phase-trace buffer for the next launches (diagnostics; null: off).
+inline long long*& gemm_trace_buffer() {
+  static long long* t = nullptr;
+  return t;
+}
+
 // Number of CTA pairs of the last pair launch (diagnostics).
 inline int& last_pair_clusters() {
   static int n = 0;
@@ -17,7 +23,9 @@ inline int& last_pair_clusters() {
 }
 
 template <int BN, bool A_MN, bool B_MN, int PASSES, int EPI, bool PAIR = false>
-void launch_t(const Params& p, dim3 grid, cudaStream_t stream) {
+void launch_t(const Params& params, dim3 grid, cudaStream_t stream) {
+  Params p = params;
+  p.trace = gemm_trace_buffer();
   // 3xTF32 stages hold A (16 KB), B and B lo: 48 KB per stage on one CTA,
   // 32 KB on a CTA pair (half of B). Pairs keep 4 stages too: 6 (with the TMEM
   // A stages recycled separately) measured slower (gemm3 0.621 vs 0.594 ms).

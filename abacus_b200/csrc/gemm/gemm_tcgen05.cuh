@@ -102,6 +102,13 @@ struct alignas(64) Params {
   // number of its rows that went there.
   const int* scatter_meta;
   int* status;
+  // Optional phase trace: CTAs 0 and 1 stamp clock64 at
+  // trace[(cta * 16 + slot) * 128 + i] for the first 128 k-tiles / chunks i:
+  // 0 TMA issued, 1 converter saw the stage, 2 converter done, 3 MMA saw the
+  // converted stage, 4 MMAs issued, 5 epilogue saw chunk i, 6 chunk i drained,
+  // converter: 7 A split in registers, 8 A stored to TMEM (issued), 9 B lo
+  // written, 10 TMEM stores complete.
+  long long* trace;
 };
 
 // Wait (bounded) until every owner of stored rows [r0, r1) of the gathered
@@ -167,6 +174,10 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+#define ABACUS_GEMM_TRACE(slot, i)                                                                   \
+  if (p.trace != nullptr && blockIdx.x < 2 && (i) < 128) {                                           \
+    p.trace[(blockIdx.x * 16 + (slot)) * 128 + (i)] = clock64();                                     \
+  }
   // Abort early (uniformly for the whole CTA) if an earlier kernel on this
   // device already recorded an error.
   // (A pair never returns early: both CTAs must reach the pair TMEM
@@ -323,6 +334,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
             break;
           }
           const int k0 = (t.kt_begin + kt) * BK;
+          ABACUS_GEMM_TRACE(0, issued)
           mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
           if (A_MN) {
 #pragma unroll
@@ -435,6 +447,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
             ok = false;
             break;
           }
+          ABACUS_GEMM_TRACE(3, it)
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
           const uint32_t a_hi = smem_u32(stage_a(s));
           const uint32_t b_hi = smem_u32(stage_b(s));
@@ -470,6 +483,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
           if (PASSES == 3 && Cfg::kAStages < STAGES) commit(&a_empty[it % Cfg::kAStages]);
           commit(&empty_bar[s]);
           if (last_in_chunk) commit(&chunk_full[buf]);
+          ABACUS_GEMM_TRACE(4, it)
           issued_any = true;
         }
         if (!ok) break;
@@ -518,6 +532,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
             dead = true;
             break;
           }
+          if (threadIdx.x == 64) ABACUS_GEMM_TRACE(5, c_idx)
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < BN / 32; ++c) {
@@ -528,6 +543,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
             for (int i = 0; i < 32; ++i) acc[c * 32 + i] += __uint_as_float(v[i]);
           }
           tc_fence_before();
+          if (threadIdx.x == 64) ABACUS_GEMM_TRACE(6, c_idx)
           if constexpr (PAIR) {
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(leader_addr(&chunk_empty[buf]));
@@ -751,6 +767,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
           ok = false;
           break;
         }
+        if (threadIdx.x == 192) ABACUS_GEMM_TRACE(1, it)
           const uint8_t* a = stage_a(s);
           uint32_t hi[BK], lo[BK];
           if (A_MN) {
@@ -763,7 +780,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
               const float x = *reinterpret_cast<const float*>(base + k * 128 + phys);
               const float h = to_tf32(x);
               hi[k] = __float_as_uint(h);
-              lo[k] = __float_as_uint(to_tf32(x - h));
+              lo[k] = __float_as_uint(to_tf32_lo(x - h));
             }
           } else {
             // Row of 128 bytes, 16-byte chunks XOR-swizzled by (row & 7).
@@ -775,7 +792,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
               for (int e = 0; e < 4; ++e) {
                 const float h = to_tf32(xs[e]);
                 hi[4 * c + e] = __float_as_uint(h);
-                lo[4 * c + e] = __float_as_uint(to_tf32(xs[e] - h));
+                lo[4 * c + e] = __float_as_uint(to_tf32_lo(xs[e] - h));
               }
             }
           }
@@ -788,9 +805,11 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
             ok = false;
             break;
           }
+          if (threadIdx.x == 192) ABACUS_GEMM_TRACE(7, it)
           tc_fence_after();
           tmem_st32(lane_addr + Cfg::kATmem + as * 2 * BK, hi);
           tmem_st32(lane_addr + Cfg::kATmem + as * 2 * BK + BK, lo);
+          if (threadIdx.x == 192) ABACUS_GEMM_TRACE(8, it)
           // B stays raw in the landing buffer (the MMA truncates it to its tf32
           // hi part); only lo is written.
           const float4* bsrc = reinterpret_cast<const float4*>(stage_b(s));
@@ -799,11 +818,15 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
     #pragma unroll 4
           for (int i = ct; i < kB4; i += 128) {
             const float4 x = bsrc[i];
-            bdst[i] = make_float4(tf32_lo_of_raw(x.x), tf32_lo_of_raw(x.y), tf32_lo_of_raw(x.z), tf32_lo_of_raw(x.w));
+            bdst[i] = make_float4(tf32_lo_of_raw_alu(x.x), tf32_lo_of_raw_alu(x.y), tf32_lo_of_raw_alu(x.z),
+                                   tf32_lo_of_raw_alu(x.w));
           }
+          if (threadIdx.x == 192) ABACUS_GEMM_TRACE(9, it)
           tmem_st_wait();
+          if (threadIdx.x == 192) ABACUS_GEMM_TRACE(10, it)
           fence_proxy_async_smem();
           tc_fence_before();
+        if (threadIdx.x == 192) ABACUS_GEMM_TRACE(2, it)
         if constexpr (PAIR) {
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(leader_addr(&conv_bar[s]));

@@ -115,6 +115,19 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, i
   return __all_sync(0xffffffffu, ok);
 }
 
+// ---------------------------------------------------------------- register split
+// Per-warpgroup register budgets (all four warps of a warpgroup execute it).
+// The increases draw on what the decreases of the other warpgroups give
+// back, within the registers the block was launched with.
+template <uint32_t N>
+__device__ __forceinline__ void regs_increase() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_decrease() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- CTA pairs
 // Two CTAs of a (2, 1, 1) cluster on neighbouring SMs share one tcgen05 MMA
 // (cta_group::2): each holds half of A's rows (and of D) and half of B's

@@ -3,8 +3,9 @@
 //
 // * One CTA computes one 128 x BN output tile.
 // * Warp 0: TMA producer. Warp 1: TMEM allocator + single-thread MMA issuer.
-//   Warps 2-5: epilogue (TMEM -> registers -> global). Warps 6-9 (3xTF32
-//   only): split-precision converter: A rows go to TMEM as hi = tf32(x) and
+//   Epilogue warpgroup (warps 2-5; 4-7 in 3xTF32 mode): TMEM -> registers ->
+//   global. Warps 8-15 (3xTF32 only, two warpgroups taking alternate
+//   k-tiles): split-precision converter: A rows go to TMEM as hi = tf32(x) and
 //   lo = tf32(x - hi); B stays raw in shared memory (the MMA reads it as its
 //   truncated tf32 hi part) and lo = tf32(x - trunc(x)) is written beside it,
 //   so the MMA warp can issue lo*hi + hi*lo + hi*hi (fp32-level accuracy).
@@ -139,7 +140,18 @@ struct Config {
   // TMEM (written by the converter), so the MMA reads A without touching smem.
   static constexpr int kStageBytes = PASSES == 3 ? kABytes + 2 * kBBytes : kABytes + kBBytes;
   static constexpr int kSmemBytes = STAGES * kStageBytes + 1024;
-  static constexpr int kThreads = PASSES == 3 ? 320 : 192;
+  // 3xTF32: warpgroup 0 = producer (warp 0) + MMA issuer (warp 1), warpgroup 1
+  // = epilogue, warpgroups 2 and 3 = converters of the even / odd k-tiles
+  // (two k-tiles are split at once: one converter's latency per k-tile is
+  // longer than the k-tile's MMAs). 1 pass: warps 0, 1 and the epilogue 2-5.
+  static constexpr int kThreads = PASSES == 3 ? 512 : 192;
+  static constexpr int kEpiWarp0 = PASSES == 3 ? 4 : 2;
+  static constexpr int kConvWarp0 = 8;
+  // Register budgets after the split (3xTF32), per thread of each warpgroup:
+  // 128 threads x (72 + 232 + 104 + 104) = 65536 = 512 threads x 128 at launch.
+  static constexpr uint32_t kRegsCtrl = 72, kRegsEpi = 232, kRegsConv = 104;
+  static_assert(PASSES != 3 || 128 * (kRegsCtrl + kRegsEpi + 2 * kRegsConv) == kThreads * 128,
+                "warpgroup register budgets must add up to the launch's 65536");
   // 3xTF32 accumulates K in chunks of kChunk k-tiles into two alternating
   // TMEM buffers that the epilogue drains (see the epilogue).
   static constexpr bool kChunked = PASSES == 3;
@@ -314,7 +326,11 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
   else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_slot;
-
+  // Register split (3xTF32), at the top of each warpgroup's branch: the
+  // epilogue holds 128 fp32 accumulators per thread, a converter a 32-element
+  // hi / lo row, warpgroup 0 only control state.
+  if (warp < Cfg::kEpiWarp0) {
+  if constexpr (PASSES == 3) regs_decrease<Cfg::kRegsCtrl>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
@@ -501,7 +517,9 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
         if (!mbar_wait(&empty_bar[j % STAGES], (j / STAGES) & 1, p.status, kStatusTimeoutEmpty)) break;
       }
     }
-  } else if (warp >= 2 && warp < 6) {
+  }  // warps 2 and 3 of warpgroup 0 (3xTF32) have no role
+  } else if (warp >= Cfg::kEpiWarp0 && warp < Cfg::kEpiWarp0 + 4) {
+    if constexpr (PASSES == 3) regs_increase<Cfg::kRegsEpi>();
     // ------------------------------------------------------------ epilogue
     const int q = warp % 4;  // TMEM lane quarter this warp may access
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
@@ -532,7 +550,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
             dead = true;
             break;
           }
-          if (threadIdx.x == 64) ABACUS_GEMM_TRACE(5, c_idx)
+          if (threadIdx.x == Cfg::kEpiWarp0 * 32) ABACUS_GEMM_TRACE(5, c_idx)
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < BN / 32; ++c) {
@@ -543,7 +561,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
             for (int i = 0; i < 32; ++i) acc[c * 32 + i] += __uint_as_float(v[i]);
           }
           tc_fence_before();
-          if (threadIdx.x == 64) ABACUS_GEMM_TRACE(6, c_idx)
+          if (threadIdx.x == Cfg::kEpiWarp0 * 32) ABACUS_GEMM_TRACE(6, c_idx)
           if constexpr (PAIR) {
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(leader_addr(&chunk_empty[buf]));
@@ -720,7 +738,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
         __threadfence_system();
         if (lane == 0) epi_ok[q] = ok ? 1 : 0;
         named_barrier_sync(1, 128);
-        if (warp == 2 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
+        if (warp == Cfg::kEpiWarp0 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
           const int owner = (m0 % p.scatter_seq) / p.scatter_chunk;
           red_release_sys_add(p.scatter_counter[owner], 1u);
         }
@@ -728,7 +746,7 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
         // Count this tile's rows per destination rank, then publish them.
         __shared__ int epi_ok[4];
         __shared__ unsigned dest_rows[8];
-        if (warp == 2 && lane < 8) dest_rows[lane] = 0u;
+        if (warp == Cfg::kEpiWarp0 && lane < 8) dest_rows[lane] = 0u;
         __threadfence_system();
         if (lane == 0) epi_ok[q] = ok ? 1 : 0;
         named_barrier_sync(1, 128);
@@ -740,19 +758,24 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
           if (lane == 0 && n) atomicAdd(&dest_rows[d], n);
         }
         named_barrier_sync(1, 128);
-        if (warp == 2 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
+        if (warp == Cfg::kEpiWarp0 && lane == 0 && epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3]) {
           for (int d = 0; d < 8; ++d)
             if (dest_rows[d]) red_release_sys_add(p.scatter_counter[d], dest_rows[d]);
         }
       }
     }
-  } else if (PASSES == 3 && warp >= 6) {
+  } else if (PASSES == 3 && warp >= Cfg::kConvWarp0) {
     // ------------------------------------------------------------ converter
     // Thread = one row of the A tile (its TMEM lane): read the row from the
     // TMA landing buffer (undoing the swizzle), split it into tf32 hi / lo and
     // store both into this stage's TMEM columns. B is split in shared memory:
-    // raw as hi, lo beside it.
-    const int ct = threadIdx.x - 192;  // 0..127
+    // raw as hi, lo beside it. Converter group g takes the k-tiles with
+    // it % 2 == g (with an even stage count, always the same stages).
+    static_assert(STAGES % 2 == 0, "two converter groups alternate over the stages");
+    regs_decrease<Cfg::kRegsConv>();
+    const int group = (warp - Cfg::kConvWarp0) / 4;
+    const int ct = threadIdx.x - Cfg::kConvWarp0 * 32 - group * 128;  // 0..127
+    const bool tracer = ct == 0;
     const int row = (warp % 4) * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>((warp % 4) * 32) << 16);
     int it = 0;
@@ -761,13 +784,14 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
       const TileInfo t = tile_at(tile);
       if (t.skip) continue;
       for (int kt = 0; kt < t.num_k; ++kt, ++it) {
+        if ((it & 1) != group) continue;
         const int s = it % STAGES;
         const int use = it / STAGES;
         if (!mbar_wait_warp(&full_bar[s], use & 1, p.status, kStatusTimeoutFull)) {
           ok = false;
           break;
         }
-        if (threadIdx.x == 192) ABACUS_GEMM_TRACE(1, it)
+        if (tracer) ABACUS_GEMM_TRACE(1, it)
           const uint8_t* a = stage_a(s);
           uint32_t hi[BK], lo[BK];
           if (A_MN) {
@@ -805,11 +829,11 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
             ok = false;
             break;
           }
-          if (threadIdx.x == 192) ABACUS_GEMM_TRACE(7, it)
+          if (tracer) ABACUS_GEMM_TRACE(7, it)
           tc_fence_after();
           tmem_st32(lane_addr + Cfg::kATmem + as * 2 * BK, hi);
           tmem_st32(lane_addr + Cfg::kATmem + as * 2 * BK + BK, lo);
-          if (threadIdx.x == 192) ABACUS_GEMM_TRACE(8, it)
+          if (tracer) ABACUS_GEMM_TRACE(8, it)
           // B stays raw in the landing buffer (the MMA truncates it to its tf32
           // hi part); only lo is written.
           const float4* bsrc = reinterpret_cast<const float4*>(stage_b(s));
@@ -821,12 +845,12 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
             bdst[i] = make_float4(tf32_lo_of_raw_alu(x.x), tf32_lo_of_raw_alu(x.y), tf32_lo_of_raw_alu(x.z),
                                    tf32_lo_of_raw_alu(x.w));
           }
-          if (threadIdx.x == 192) ABACUS_GEMM_TRACE(9, it)
+          if (tracer) ABACUS_GEMM_TRACE(9, it)
           tmem_st_wait();
-          if (threadIdx.x == 192) ABACUS_GEMM_TRACE(10, it)
+          if (tracer) ABACUS_GEMM_TRACE(10, it)
           fence_proxy_async_smem();
           tc_fence_before();
-        if (threadIdx.x == 192) ABACUS_GEMM_TRACE(2, it)
+        if (tracer) ABACUS_GEMM_TRACE(2, it)
         if constexpr (PAIR) {
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(leader_addr(&conv_bar[s]));

@@ -9,6 +9,10 @@ void gemm_out(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, b
               int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate, int64_t passes);
 int64_t gemm_n_tiles(int64_t n, int64_t passes);
 int64_t gemm_pair_clusters();
+void gemm_qkv_norm_rope(torch::Tensor qkv, torch::Tensor x, std::vector<torch::Tensor> ws, torch::Tensor q,
+                        torch::Tensor k, torch::Tensor rstd, torch::Tensor q_gamma, torch::Tensor k_gamma,
+                        torch::Tensor cos_t, torch::Tensor sin_t, int64_t seq_len, int64_t heads, int64_t head_dim,
+                        double eps, int64_t passes);
 void gemm_trace(c10::optional<torch::Tensor> buf);
 int64_t gemm_grouped(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
                      int64_t b_mode, double alpha, bool accumulate, int64_t passes,

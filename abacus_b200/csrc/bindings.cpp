@@ -9,6 +9,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_out", &abacus::gemm::gemm_out, "tcgen05 tf32 / 3xTF32 GEMM into C");
   m.def("gemm_n_tiles", &abacus::gemm::gemm_n_tiles, "N tiles of a single-B GEMM of the given output width");
   m.def("gemm_pair_clusters", &abacus::gemm::gemm_pair_clusters, "CTA pairs of the last CTA-pair GEMM launch");
+  m.def("gemm_qkv_norm_rope", &abacus::gemm::gemm_qkv_norm_rope,
+        "QKV projection with QK-norm + RoPE fused into the GEMM epilogue");
   m.def("gemm_trace", &abacus::gemm::gemm_trace, "phase trace of the following GEMM launches (None: off)");
   m.def("gemm_grouped", &abacus::gemm::gemm_grouped, "one GEMM launch over (experts, rows, cols) operands");
   m.def("gemm_swiglu_grouped", &abacus::gemm::gemm_swiglu_grouped, "grouped gate/up GEMM with SwiGLU epilogue");

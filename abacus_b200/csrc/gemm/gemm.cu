@@ -200,9 +200,17 @@ Comm make_comm(const c10::optional<std::vector<int64_t>>& wait, const c10::optio
   return c;
 }
 
+// Device pointers and sizes of the QK-norm + RoPE epilogue (Params::q_out ...).
+struct QKFuse {
+  float *q_out, *k_out, *rstd;
+  const float *q_gamma, *k_gamma, *cos_t, *sin_t;
+  int seq_len, heads, head_dim;
+  float eps;
+};
+
 int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
                       int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate,
-                      int64_t passes, const Comm& cm);
+                      int64_t passes, const Comm& cm, const QKFuse* qk = nullptr);
 void gemm_swiglu_impl(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up, torch::Tensor g, torch::Tensor u,
                       torch::Tensor h, int64_t passes, const Comm& cm);
 void gemm_swiglu_bwd_impl(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g, torch::Tensor u, torch::Tensor dgu,
@@ -234,6 +242,44 @@ void gemm_trace(c10::optional<torch::Tensor> buf) {
   gemm_trace_buffer() = reinterpret_cast<long long*>(buf->data_ptr<int64_t>());
 }
 
+// [q | k | v] = x @ [Wq | Wk | Wv] with QK-norm + RoPE in the epilogue:
+// qkv (T, 3HK) raw, q / k (T, HK) normalised and rotated, rstd (T * 2 * H).
+// gammas (head_dim,), cos / sin (P, head_dim / 2) with P > the positions used
+// (row % seq_len).
+void gemm_qkv_norm_rope(torch::Tensor qkv, torch::Tensor x, std::vector<torch::Tensor> ws, torch::Tensor q,
+                        torch::Tensor k, torch::Tensor rstd, torch::Tensor q_gamma, torch::Tensor k_gamma,
+                        torch::Tensor cos_t, torch::Tensor sin_t, int64_t seq_len, int64_t heads, int64_t head_dim,
+                        double eps, int64_t passes) {
+  const int64_t t = x.size(0), hk = heads * head_dim;
+  for (auto* o : {&q, &k}) {
+    TORCH_CHECK(o->is_cuda() && o->scalar_type() == torch::kFloat32 && o->is_contiguous() && o->size(0) == t &&
+                    o->size(1) == hk && reinterpret_cast<uintptr_t>(o->data_ptr()) % 16 == 0,
+                "q / k outputs: contiguous (T, heads * head_dim) fp32");
+  }
+  TORCH_CHECK(rstd.is_contiguous() && rstd.numel() == t * 2 * heads, "rstd: T * 2 * heads");
+  for (auto* g : {&q_gamma, &k_gamma})
+    TORCH_CHECK(g->is_contiguous() && g->numel() == head_dim && reinterpret_cast<uintptr_t>(g->data_ptr()) % 16 == 0,
+                "gammas: contiguous (head_dim,)");
+  for (auto* tb : {&cos_t, &sin_t})
+    TORCH_CHECK(tb->is_contiguous() && tb->dim() == 2 && tb->size(1) == head_dim / 2 && tb->size(0) >= seq_len &&
+                    reinterpret_cast<uintptr_t>(tb->data_ptr()) % 16 == 0,
+                "cos / sin tables: contiguous (positions >= seq_len, head_dim / 2)");
+  TORCH_CHECK(seq_len > 0, "seq_len");
+  QKFuse f;
+  f.q_out = q.data_ptr<float>();
+  f.k_out = k.data_ptr<float>();
+  f.rstd = rstd.data_ptr<float>();
+  f.q_gamma = q_gamma.data_ptr<float>();
+  f.k_gamma = k_gamma.data_ptr<float>();
+  f.cos_t = cos_t.data_ptr<float>();
+  f.sin_t = sin_t.data_ptr<float>();
+  f.seq_len = static_cast<int>(seq_len);
+  f.heads = static_cast<int>(heads);
+  f.head_dim = static_cast<int>(head_dim);
+  f.eps = static_cast<float>(eps);
+  (void)gemm_out_impl(qkv, x, ws, false, false, kBSegN, 1.0, c10::nullopt, false, passes, Comm{}, &f);
+}
+
 // Number of N tiles a single-B GEMM of output width n uses (stores per row).
 int64_t gemm_n_tiles(int64_t n, int64_t passes) {
   check_passes(passes);
@@ -255,7 +301,7 @@ int64_t gemm_out_tp(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor>
 namespace {
 int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tensor> bs, bool trans_a, bool trans_b,
                       int64_t b_mode, double alpha, c10::optional<torch::Tensor> residual, bool accumulate,
-                      int64_t passes, const Comm& cm) {
+                      int64_t passes, const Comm& cm, const QKFuse* qk) {
   check_passes(passes);
   TORCH_CHECK(!bs.empty() && bs.size() <= 3, "between 1 and 3 B operands");
   const c10::cuda::CUDAGuard guard(a.device());
@@ -321,12 +367,32 @@ int64_t gemm_out_impl(torch::Tensor c, torch::Tensor a, std::vector<torch::Tenso
   p.accumulate = accumulate ? 1 : 0;
   p.status = host::status_ptr(a.device().index());
   apply_comm(p, cm, A.mn_major, B[0].mn_major);
+  if (qk != nullptr) {
+    TORCH_CHECK(passes == 3 && b_mode == kBSegN && bs.size() == 3 && BN == 128 && seg % BN == 0, "fused QK-norm "
+                "+ RoPE needs the 3xTF32 N-segmented [q | k | v] GEMM with 128-column segments");
+    TORCH_CHECK(qk->head_dim == 64 || qk->head_dim == 128, "fused QK-norm + RoPE: head_dim 64 or 128");
+    TORCH_CHECK(!residual && !accumulate && alpha == 1.0 && cm.wait.empty() && cm.scatter.empty(),
+                "fused QK-norm + RoPE takes a plain store");
+    TORCH_CHECK(seg == static_cast<int64_t>(qk->heads) * qk->head_dim, "segment width must be heads * head_dim");
+    p.q_out = qk->q_out;
+    p.k_out = qk->k_out;
+    p.qk_rstd = qk->rstd;
+    p.q_gamma = qk->q_gamma;
+    p.k_gamma = qk->k_gamma;
+    p.rope_cos = qk->cos_t;
+    p.rope_sin = qk->sin_t;
+    p.seq_len = qk->seq_len;
+    p.heads = qk->heads;
+    p.head_dim = qk->head_dim;
+    p.qk_cols = static_cast<int>(seg);
+    p.qk_eps = qk->eps;
+  }
   const long long tiles = ((M + BM - 1) / BM) * p.num_n_tiles;
   // Work units: 128-row tiles, or 256-row tiles of a CTA pair.
   const long long units = pair ? ((M + 2 * BM - 1) / (2 * BM)) * p.num_n_tiles : tiles;
   const int k_tiles = static_cast<int>((K + BK - 1) / BK);
   const int sms = at::cuda::getDeviceProperties(a.device().index())->multiProcessorCount;
-  int splits = (N % 4 == 0 && !scatter) ? pick_splits(units, k_tiles, pair ? sms / 2 : sms) : 1;
+  int splits = (N % 4 == 0 && !scatter && qk == nullptr) ? pick_splits(units, k_tiles, pair ? sms / 2 : sms) : 1;
   auto stream = at::cuda::getCurrentCUDAStream();
   p.k_tiles_per_split = (k_tiles + splits - 1) / splits;
   splits = (k_tiles + p.k_tiles_per_split - 1) / p.k_tiles_per_split;

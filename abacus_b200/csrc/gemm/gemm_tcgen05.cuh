@@ -22,6 +22,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <type_traits>
 #include "../common/sm100.cuh"
 
 namespace abacus {
@@ -103,6 +104,23 @@ struct alignas(64) Params {
   // number of its rows that went there.
   const int* scatter_meta;
   int* status;
+  // QK-norm + RoPE fused into the QKV projection (3xTF32 store epilogue of an
+  // N-segmented [q | k | v] GEMM, qk_cols = H * head_dim columns per segment):
+  // for the q and k tiles each row's heads are RMS-normalised over head_dim
+  // (eps, gamma q_gamma / k_gamma), rotated (rotate-half pairs (i, i + hd/2),
+  // cos / sin tables (P, hd/2) at position positions[row] or row % seq_len)
+  // and stored to q_out / k_out (T, qk_cols); rstd[(row * 2 + which) * heads +
+  // head] keeps 1 / rms for the backward. The raw projection is stored as usual.
+  float* q_out;
+  float* k_out;
+  float* qk_rstd;
+  const float* q_gamma;
+  const float* k_gamma;
+  const float* rope_cos;
+  const float* rope_sin;
+  const int64_t* positions;
+  int seq_len, heads, head_dim, qk_cols;
+  float qk_eps;
   // Optional phase trace: CTAs 0 and 1 stamp clock64 at
   // trace[(cta * 16 + slot) * 128 + i] for the first 128 k-tiles / chunks i:
   // 0 TMA issued, 1 converter saw the stage, 2 converter done, 3 MMA saw the
@@ -642,6 +660,50 @@ __global__ void __launch_bounds__(Config<BN, A_MN, B_MN, PASSES, STAGES, PAIR>::
                 }
               }
             }
+          }
+        }
+        if constexpr (Cfg::kChunked) {
+          if (p.q_out != nullptr && row_ok && n0 < 2 * p.qk_cols) {
+            // The tile's whole row is in acc: normalise and rotate its heads.
+            const int which = n0 >= p.qk_cols ? 1 : 0;
+            const long long pos = p.positions ? p.positions[row] : static_cast<long long>(row % p.seq_len);
+            auto heads_of_row = [&](auto hd_c) {
+              constexpr int HD = decltype(hd_c)::value, HALF = HD / 2;
+              const float* gamma = which ? p.k_gamma : p.q_gamma;
+              const float* cs = p.rope_cos + pos * HALF;
+              const float* sn = p.rope_sin + pos * HALF;
+#pragma unroll
+              for (int j = 0; j < BN / HD; ++j) {
+                float ss = 0.f;
+#pragma unroll
+                for (int i = 0; i < HD; ++i) ss = fmaf(acc[j * HD + i], acc[j * HD + i], ss);
+                const float r = rsqrtf(ss / HD + p.qk_eps);
+                const int head = (n0 - which * p.qk_cols) / HD + j;
+                p.qk_rstd[(static_cast<long long>(row) * 2 + which) * p.heads + head] = r;
+                float* dst = (which ? p.k_out : p.q_out) + static_cast<long long>(row) * p.qk_cols + head * HD;
+#pragma unroll
+                for (int i = 0; i < HALF; i += 4) {
+                  const float4 c4 = *reinterpret_cast<const float4*>(cs + i);
+                  const float4 s4 = *reinterpret_cast<const float4*>(sn + i);
+                  const float4 g1 = *reinterpret_cast<const float4*>(gamma + i);
+                  const float4 g2 = *reinterpret_cast<const float4*>(gamma + HALF + i);
+                  const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+                  const float ga[4] = {g1.x, g1.y, g1.z, g1.w}, gb[4] = {g2.x, g2.y, g2.z, g2.w};
+                  float o1[4], o2[4];
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float n1 = ga[e] * acc[j * HD + i + e] * r;
+                    const float n2 = gb[e] * acc[j * HD + HALF + i + e] * r;
+                    o1[e] = n1 * cv[e] - n2 * sv[e];
+                    o2[e] = n2 * cv[e] + n1 * sv[e];
+                  }
+                  *reinterpret_cast<float4*>(dst + i) = make_float4(o1[0], o1[1], o1[2], o1[3]);
+                  *reinterpret_cast<float4*>(dst + HALF + i) = make_float4(o2[0], o2[1], o2[2], o2[3]);
+                }
+              }
+            };
+            if (p.head_dim == 64) heads_of_row(std::integral_constant<int, 64>{});
+            else heads_of_row(std::integral_constant<int, 128>{});
           }
         }
       } else if (ok && EPI == kEpiSwiGLU) {

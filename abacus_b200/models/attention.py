@@ -159,10 +159,8 @@ class MultiHeadAttention(torch.nn.Module):
 
     def _forward_fused(self, x_BLD, rotary, residual):
         b, length, _ = x_BLD.shape
-        qkv = gemm.qkv_projection(x_BLD, self.w_q_DHK, self.w_k_DHK, self.w_v_DHK)
-        o = attn_ops.causal_attention(
-            qkv, b, self.local_heads, self.head_dim, self.q_norm.gamma(), self.k_norm.gamma(), rotary.inv_freq
-        )
+        o = attn_ops.qkv_attention(x_BLD, self.w_q_DHK, self.w_k_DHK, self.w_v_DHK, b, self.local_heads,
+                                   self.head_dim, self.q_norm.gamma(), self.k_norm.gamma(), rotary.inv_freq)
         w_o = self.w_o_HKD.reshape(self.local_heads * self.head_dim, self.dim)
         res2 = None if residual is None else residual.reshape(-1, self.dim)
         return gemm.linear(o, w_o, res2).view(b, length, self.dim)

@@ -11,7 +11,8 @@ O-projection GEMM reads. Semantics (``abacus/attention.py:118-150,175-213``):
 * scores are scaled by 1/sqrt(head_dim) and masked where key position >
   query position (global positions under context parallelism).
 
-CUDA: the prologue kernel writes rotated q and k once, then the tcgen05
+CUDA: ``qkv_attention`` normalises and rotates q and k in the QKV GEMM's
+epilogue (fp32 mode; otherwise a prologue kernel writes them once), then the tcgen05
 flash-attention kernels (``csrc/attention``) compute the output without ever
 materialising the (L, L) score matrix; backward recomputes the scores tile by
 tile. CPU: the reference's materialised formulation.
@@ -19,10 +20,11 @@ tile. CPU: the reference's materialised formulation.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
-from abacus_b200.ops import precision
+from abacus_b200.ops import gemm, precision
 from abacus_b200.ops._ext import ext
 from abacus_b200.ops.norm import EPS, rmsnorm_reference
 
@@ -96,20 +98,55 @@ class _QKPrologue(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dq, dk, dv):
         qkv, q_gamma, k_gamma, cos_t, sin_t, positions, rstd = ctx.saved_tensors
-        heads, head_dim, seq_len = ctx.dims
-        hk = heads * head_dim
-        dqkv = torch.zeros_like(qkv) if dq is None or dk is None else torch.empty_like(qkv)
-        dq = torch.zeros(qkv.shape[0], hk, device=qkv.device) if dq is None else dq.contiguous()
-        dk = torch.zeros(qkv.shape[0], hk, device=qkv.device) if dk is None else dk.contiguous()
-        dgq = torch.empty_like(q_gamma)
-        dgk = torch.empty_like(k_gamma)
-        ext().qk_prologue_bwd(qkv, q_gamma, k_gamma, cos_t, sin_t, positions, seq_len, dq, dk, rstd, dqkv, dgq, dgk,
-                              heads, head_dim)
-        if dv is None:
-            dqkv[:, 2 * hk :] = 0.0
-        else:
-            dqkv[:, 2 * hk :].copy_(dv)
+        dqkv, dgq, dgk = _prologue_grads(qkv, q_gamma, k_gamma, cos_t, sin_t, positions, rstd, dq, dk, dv, *ctx.dims)
         return dqkv, dgq, dgk, None, None, None, None, None, None
+
+
+def _prologue_grads(qkv, q_gamma, k_gamma, cos_t, sin_t, positions, rstd, dq, dk, dv, heads, head_dim, seq_len):
+    """d(qkv) and the gamma gradients from dq, dk (rotated, normalised) and dv."""
+    hk = heads * head_dim
+    dqkv = torch.zeros_like(qkv) if dq is None or dk is None else torch.empty_like(qkv)
+    dq = torch.zeros(qkv.shape[0], hk, device=qkv.device) if dq is None else dq.contiguous()
+    dk = torch.zeros(qkv.shape[0], hk, device=qkv.device) if dk is None else dk.contiguous()
+    dgq = torch.empty_like(q_gamma)
+    dgk = torch.empty_like(k_gamma)
+    ext().qk_prologue_bwd(qkv, q_gamma, k_gamma, cos_t, sin_t, positions, seq_len, dq, dk, rstd, dqkv, dgq, dgk,
+                          heads, head_dim)
+    if dv is None:
+        dqkv[:, 2 * hk :] = 0.0
+    else:
+        dqkv[:, 2 * hk :].copy_(dv)
+    return dqkv, dgq, dgk
+
+
+class _QKVNormRope(torch.autograd.Function):
+    """x -> (q, k, v) in one GEMM: the N-segmented QKV projection whose 3xTF32
+    epilogue also RMS-normalises and rotates each q / k head of the row it
+    holds, so the separate prologue pass over qkv disappears. The backward is
+    the prologue backward followed by the projection's gradients."""
+
+    @staticmethod
+    def forward(ctx, x, wq, wk, wv, q_gamma, k_gamma, cos_t, sin_t, heads, head_dim, seq_len):
+        x2 = x.reshape(-1, x.shape[-1])
+        ws = [w.reshape(w.shape[0], -1) for w in (wq, wk, wv)]
+        t, hk = x2.shape[0], heads * head_dim
+        qkv = torch.empty(t, 3 * hk, device=x.device, dtype=torch.float32)
+        q = torch.empty(t, hk, device=x.device, dtype=torch.float32)
+        k = torch.empty_like(q)
+        rstd = torch.empty(t * 2 * heads, device=x.device, dtype=torch.float32)
+        ext().gemm_qkv_norm_rope(qkv, x2, ws, q, k, rstd, q_gamma, k_gamma, cos_t, sin_t, seq_len, heads, head_dim,
+                                 EPS, precision.passes())
+        ctx.save_for_backward(x2, wq, wk, wv, qkv, q_gamma, k_gamma, cos_t, sin_t, rstd)
+        ctx.dims = (heads, head_dim, seq_len)
+        ctx.x_shape = x.shape
+        return q, k, qkv.narrow(1, 2 * hk, hk)
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        x2, wq, wk, wv, qkv, q_gamma, k_gamma, cos_t, sin_t, rstd = ctx.saved_tensors
+        dqkv, dgq, dgk = _prologue_grads(qkv, q_gamma, k_gamma, cos_t, sin_t, None, rstd, dq, dk, dv, *ctx.dims)
+        dx, dwq, dwk, dwv = gemm.qkv_projection_grads(x2, wq, wk, wv, dqkv)
+        return dx.reshape(ctx.x_shape), dwq, dwk, dwv, dgq, dgk, None, None, None, None, None
 
 
 class _Flash(torch.autograd.Function):
@@ -227,6 +264,26 @@ def flash_attention(q, k, v, batch, heads, head_dim, q_pos=None, k_pos=None):
                 f"head_dim {head_dim} in fp32 mode supports plain causal attention only (no positions)")
         return _DenseCausal.apply(q, k, v, batch, heads, head_dim)
     return _Flash.apply(q, k, v, q_pos, k_pos, batch, heads, head_dim)
+
+
+def _fused_qk_usable(x: torch.Tensor, heads: int, head_dim: int, inv_freq) -> bool:
+    return (x.is_cuda and inv_freq is not None and precision.passes() == 3 and head_dim in (64, 128)
+            and (heads * head_dim) % 128 == 0 and os.environ.get("ABACUS_FUSED_QK", "1") != "0")
+
+
+def qkv_attention(x, wq, wk, wv, batch, heads, head_dim, q_gamma, k_gamma, inv_freq):
+    """x (..., D) -> (T, HK) attention output: QKV projection, QK-norm,
+    RoPE and causal attention. On CUDA in fp32 mode the norm and rotation run
+    in the projection GEMM's epilogue (``ABACUS_FUSED_QK=0``: separate
+    prologue kernel); otherwise as ``causal_attention`` over the projection."""
+    if _fused_qk_usable(x, heads, head_dim, inv_freq):
+        seq_len = (x.numel() // x.shape[-1]) // batch
+        cos_t, sin_t = _cached_tables(inv_freq, seq_len)
+        q, k, v = _QKVNormRope.apply(x.contiguous(), wq, wk, wv, q_gamma.contiguous(), k_gamma.contiguous(), cos_t,
+                                     sin_t, heads, head_dim, seq_len)
+        return flash_attention(q, k, v, batch, heads, head_dim)
+    qkv = gemm.qkv_projection(x, wq, wk, wv)
+    return causal_attention(qkv, batch, heads, head_dim, q_gamma, k_gamma, inv_freq)
 
 
 def causal_attention(

@@ -263,17 +263,25 @@ class _QKVProjection(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dqkv):
         x2, wq, wk, wv = ctx.saved_tensors
-        dqkv = dqkv.contiguous()
-        ws = [w.reshape(w.shape[0], -1) for w in (wq, wk, wv)]
-        hk = ws[0].shape[1]
-        if hk % 32 == 0:
-            dx = matmul(dqkv, ws, trans_b=True, b_mode=B_SEG_K)
-        else:
-            dx = matmul(dqkv[:, :hk].contiguous(), ws[0], trans_b=True)
-            for i in (1, 2):
-                matmul(dqkv[:, i * hk : (i + 1) * hk].contiguous(), ws[i], trans_b=True, out=dx, accumulate=True)
-        grads = [matmul(x2, dqkv[:, i * hk : (i + 1) * hk], trans_a=True).view_as(w) for i, w in enumerate((wq, wk, wv))]
+        dx, *grads = qkv_projection_grads(x2, wq, wk, wv, dqkv)
         return (dx.reshape(ctx.x_shape), *grads)
+
+
+def qkv_projection_grads(x2, wq, wk, wv, dqkv):
+    """Gradients of ``[x @ Wq | x @ Wk | x @ Wv]`` given dqkv (T, 3*HK):
+    dx (T, D) as one K-segmented GEMM, then dWq, dWk, dWv in their (D, H, K)
+    shapes."""
+    dqkv = dqkv.contiguous()
+    ws = [w.reshape(w.shape[0], -1) for w in (wq, wk, wv)]
+    hk = ws[0].shape[1]
+    if hk % 32 == 0:
+        dx = matmul(dqkv, ws, trans_b=True, b_mode=B_SEG_K)
+    else:
+        dx = matmul(dqkv[:, :hk].contiguous(), ws[0], trans_b=True)
+        for i in (1, 2):
+            matmul(dqkv[:, i * hk : (i + 1) * hk].contiguous(), ws[i], trans_b=True, out=dx, accumulate=True)
+    grads = [matmul(x2, dqkv[:, i * hk : (i + 1) * hk], trans_a=True).view_as(w) for i, w in enumerate((wq, wk, wv))]
+    return (dx, *grads)
 
 
 def qkv_projection(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor) -> torch.Tensor:

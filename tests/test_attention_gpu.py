@@ -154,3 +154,36 @@ def test_dense_head_dim_128_fp32_forward_backward(batch, length, heads):
     assert _err(out.detach().cpu(), ref_o) < 2e-5
     for got, want in ((q.grad, rq), (k.grad, rk), (v.grad, rv)):
         assert _err(got.cpu(), want) < 5e-5
+
+
+@pytest.mark.parametrize("heads,hd,length", [(4, 64, 256), (2, 128, 384)])
+def test_qkv_gemm_with_fused_qk_norm_rope(monkeypatch, heads, hd, length):
+    """QK-norm + RoPE in the QKV GEMM epilogue against the separate prologue
+    kernel (outputs and all gradients) and against the fp64 reference."""
+    precision.set_precision("fp32")
+    torch.manual_seed(21)
+    batch, dim = 2, 256
+    x = torch.randn(batch, length, dim, device="cuda")
+    w = [torch.randn(dim, heads, hd, device="cuda") / dim**0.5 for _ in range(3)]
+    gq = 1 + 0.1 * torch.randn(hd, device="cuda")
+    gk = 1 + 0.1 * torch.randn(hd, device="cuda")
+    inv_freq = 1.0 / (10000 ** (torch.arange(0, hd, 2, device="cuda").float() / hd))
+    gout = torch.randn(batch * length, heads * hd, device="cuda")
+    results = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("ABACUS_FUSED_QK", flag)
+        leaves = [t.clone().requires_grad_() for t in [x, *w, gq, gk]]
+        out = attn_ops.qkv_attention(leaves[0], leaves[1], leaves[2], leaves[3], batch, heads, hd, leaves[4],
+                                     leaves[5], inv_freq)
+        out.backward(gout)
+        torch.cuda.synchronize()
+        check_status()
+        results[flag] = [out.detach()] + [t.grad for t in leaves]
+    for fused, split in zip(results["1"], results["0"]):
+        assert _err(fused, split) < 1e-5
+    # fp64 reference of the whole path
+    xd, wqd, wkd, wvd, gqd, gkd = [t.double() for t in [x, *w, gq, gk]]
+    qkv = torch.cat([xd.reshape(-1, dim) @ m.reshape(dim, -1) for m in (wqd, wkd, wvd)], dim=1)
+    pos = torch.arange(length, device="cuda")
+    ref = attn_ops.attention_reference(qkv, batch, heads, hd, gqd, gkd, inv_freq.double(), pos, pos)
+    assert _err(results["1"][0], ref) < 2e-5

@@ -137,6 +137,117 @@ int grid_for(long long tokens, const torch::Device& dev) {
     default: TORCH_CHECK(false, "router kernels support 1, 2, 4, 8, 16, 32 or 64 experts"); \
   }
 
+// ---------------------------------------------------------------- routing
+// One thread per token (E <= 64 logits in registers). Probabilities are the
+// softmax over the experts (mode 0) or the per-expert sigmoid (mode 1); the
+// top_k experts are chosen by probability (softmax) or by probability +
+// selection bias (sigmoid; the bias only steers selection), ties going to the
+// lower expert index; their probabilities, renormalised to sum 1 and scaled
+// by route_scale, are the routing weights.
+template <int E>
+__global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                                                         int mode, int top_k, float route_scale, int tokens,
+                                                         float* __restrict__ probs, float* __restrict__ weights,
+                                                         int64_t* __restrict__ indices) {
+  const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= tokens) return;
+  float pr[E];
+  const float* row = logits + t * E;
+  if (mode == 0) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      pr[e] = row[e];
+      m = fmaxf(m, pr[e]);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      pr[e] = __expf(pr[e] - m);
+      sum += pr[e];
+    }
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int e = 0; e < E; ++e) pr[e] *= inv;
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) pr[e] = 1.f / (1.f + __expf(-row[e]));
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) probs[t * E + e] = pr[e];
+  // Selection: top_k passes of an argmax over the not yet chosen experts.
+  unsigned long long chosen = 0ull;
+  float picked_sum = 0.f;
+  for (int k = 0; k < top_k; ++k) {
+    int best = -1;
+    float best_v = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float v = pr[e] + (mode == 1 && bias != nullptr ? bias[e] : 0.f);
+      if (!((chosen >> e) & 1ull) && (best < 0 || v > best_v)) {
+        best = e;
+        best_v = v;
+      }
+    }
+    chosen |= 1ull << best;
+    indices[t * top_k + k] = best;
+    float pb = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) pb = e == best ? pr[e] : pb;
+    weights[t * top_k + k] = pb;
+    picked_sum += pb;
+  }
+  const float scale = route_scale / picked_sum;
+  for (int k = 0; k < top_k; ++k) weights[t * top_k + k] *= scale;
+}
+
+// dlogits from the gradients of the routing weights (and of the probabilities,
+// for the auxiliary loss): with S the chosen experts' probability sum,
+// d p_i = route_scale * (dw_i / S - sum_j dw_j p_j / S^2) for chosen i, plus
+// dprobs; then through the softmax (p_e (g_e - sum_f g_f p_f)) or the sigmoid
+// (g_e p_e (1 - p_e)).
+template <int E>
+__global__ void __launch_bounds__(256) route_topk_bwd_kernel(const float* __restrict__ probs,
+                                                             const int64_t* __restrict__ indices,
+                                                             const float* __restrict__ dweights,
+                                                             const float* __restrict__ dprobs, int mode, int top_k,
+                                                             float route_scale, int tokens,
+                                                             float* __restrict__ dlogits) {
+  const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= tokens) return;
+  float pr[E], g[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    pr[e] = probs[t * E + e];
+    g[e] = dprobs ? dprobs[t * E + e] : 0.f;
+  }
+  float s = 0.f, dot = 0.f;
+  for (int k = 0; k < top_k; ++k) {
+    const int i = static_cast<int>(indices[t * top_k + k]);
+    float pi = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) pi = e == i ? pr[e] : pi;
+    s += pi;
+    dot += dweights[t * top_k + k] * pi;
+  }
+  for (int k = 0; k < top_k; ++k) {
+    const int i = static_cast<int>(indices[t * top_k + k]);
+    const float add = route_scale * (dweights[t * top_k + k] / s - dot / (s * s));
+#pragma unroll
+    for (int e = 0; e < E; ++e) g[e] += e == i ? add : 0.f;
+  }
+  if (mode == 0) {
+    float gp = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) gp += g[e] * pr[e];
+#pragma unroll
+    for (int e = 0; e < E; ++e) dlogits[t * E + e] = pr[e] * (g[e] - gp);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) dlogits[t * E + e] = g[e] * pr[e] * (1.f - pr[e]);
+  }
+}
+
 }  // namespace
 
 void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor logits) {
@@ -197,6 +308,73 @@ void router_logits_bwd(torch::Tensor dlogits, torch::Tensor x, torch::Tensor w, 
   router_dw_reduce_kernel<<<(n + 255) / 256, 256, 0, s>>>(partial.data_ptr<float>(), dw.data_ptr<float>(), slabs, n);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   abacus::host::note_launch(3);
+}
+
+}  // namespace ops
+}  // namespace abacus
+
+namespace abacus {
+namespace ops {
+
+void route_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_t mode, int64_t top_k,
+                double route_scale, torch::Tensor probs, torch::Tensor weights, torch::Tensor indices) {
+  const c10::cuda::CUDAGuard guard(logits.device());
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == torch::kFloat32 && logits.is_contiguous() && logits.dim() == 2,
+              "logits: contiguous (tokens, E) fp32");
+  const int tokens = static_cast<int>(logits.size(0)), experts = static_cast<int>(logits.size(1));
+  TORCH_CHECK(mode == 0 || mode == 1, "mode: 0 softmax, 1 sigmoid");
+  TORCH_CHECK(top_k >= 1 && top_k <= experts, "top_k in [1, E]");
+  TORCH_CHECK(probs.is_contiguous() && probs.sizes() == logits.sizes(), "probs: (tokens, E)");
+  TORCH_CHECK(weights.is_contiguous() && weights.scalar_type() == torch::kFloat32 && weights.numel() == tokens * top_k,
+              "weights: (tokens, top_k) fp32");
+  TORCH_CHECK(indices.is_contiguous() && indices.scalar_type() == torch::kInt64 && indices.numel() == tokens * top_k,
+              "indices: (tokens, top_k) int64");
+  const float* b = nullptr;
+  if (bias) {
+    TORCH_CHECK(bias->is_cuda() && bias->scalar_type() == torch::kFloat32 && bias->is_contiguous() &&
+                    bias->numel() == experts,
+                "bias: (E,) fp32");
+    b = bias->data_ptr<float>();
+  }
+  if (tokens == 0) return;
+  auto s = at::cuda::getCurrentCUDAStream();
+  const int grid = (tokens + 255) / 256;
+  ABACUS_ROUTER_DISPATCH(experts, {
+    route_topk_kernel<kE><<<grid, 256, 0, s>>>(logits.data_ptr<float>(), b, static_cast<int>(mode),
+                                               static_cast<int>(top_k), static_cast<float>(route_scale), tokens,
+                                               probs.data_ptr<float>(), weights.data_ptr<float>(),
+                                               indices.data_ptr<int64_t>());
+  })
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
+}
+
+void route_topk_bwd(torch::Tensor probs, torch::Tensor indices, torch::Tensor dweights,
+                    c10::optional<torch::Tensor> dprobs, int64_t mode, int64_t top_k, double route_scale,
+                    torch::Tensor dlogits) {
+  const c10::cuda::CUDAGuard guard(probs.device());
+  TORCH_CHECK(probs.is_contiguous() && probs.dim() == 2 && probs.scalar_type() == torch::kFloat32, "probs");
+  const int tokens = static_cast<int>(probs.size(0)), experts = static_cast<int>(probs.size(1));
+  TORCH_CHECK(indices.is_contiguous() && indices.numel() == tokens * top_k && indices.scalar_type() == torch::kInt64,
+              "indices");
+  TORCH_CHECK(dweights.is_contiguous() && dweights.numel() == tokens * top_k, "dweights");
+  TORCH_CHECK(dlogits.is_contiguous() && dlogits.sizes() == probs.sizes(), "dlogits");
+  const float* dp = nullptr;
+  if (dprobs) {
+    TORCH_CHECK(dprobs->is_contiguous() && dprobs->sizes() == probs.sizes(), "dprobs");
+    dp = dprobs->data_ptr<float>();
+  }
+  if (tokens == 0) return;
+  auto s = at::cuda::getCurrentCUDAStream();
+  const int grid = (tokens + 255) / 256;
+  ABACUS_ROUTER_DISPATCH(experts, {
+    route_topk_bwd_kernel<kE><<<grid, 256, 0, s>>>(probs.data_ptr<float>(), indices.data_ptr<int64_t>(),
+                                                   dweights.data_ptr<float>(), dp, static_cast<int>(mode),
+                                                   static_cast<int>(top_k), static_cast<float>(route_scale), tokens,
+                                                   dlogits.data_ptr<float>());
+  })
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
 }
 
 }  // namespace ops

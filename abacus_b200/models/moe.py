@@ -111,6 +111,40 @@ def router_logits(x_BLD: torch.Tensor, w_DE: torch.Tensor) -> torch.Tensor:
     return x_BLD @ w_DE
 
 
+class _RouteTopK(torch.autograd.Function):
+    """Routing on one kernel per direction: probabilities, top-k selection and
+    renormalised weights (forward); d logits from d weights and d probs
+    (backward). Returns (weights, indices, probs)."""
+
+    @staticmethod
+    def forward(ctx, logits_TE, bias_E, mode, top_k, route_scale):
+        t, e = logits_TE.shape
+        probs = torch.empty_like(logits_TE)
+        weights = torch.empty(t, top_k, device=logits_TE.device, dtype=torch.float32)
+        indices = torch.empty(t, top_k, device=logits_TE.device, dtype=torch.int64)
+        ext().route_topk(logits_TE, bias_E, mode, top_k, route_scale, probs, weights, indices)
+        ctx.save_for_backward(probs, indices)
+        ctx.meta = (mode, top_k, route_scale)
+        ctx.mark_non_differentiable(indices)
+        return weights, indices, probs
+
+    @staticmethod
+    def backward(ctx, d_weights, _d_indices, d_probs):
+        probs, indices = ctx.saved_tensors
+        mode, top_k, route_scale = ctx.meta
+        if d_weights is None:
+            d_weights = torch.zeros(indices.shape, device=probs.device, dtype=torch.float32)
+        d_logits = torch.empty_like(probs)
+        ext().route_topk_bwd(probs, indices, d_weights.contiguous(), None if d_probs is None else d_probs.contiguous(),
+                             mode, top_k, route_scale, d_logits)
+        return d_logits, None, None, None, None
+
+
+def _route_kernel_usable(logits_BLE: torch.Tensor) -> bool:
+    e = logits_BLE.shape[-1]
+    return logits_BLE.is_cuda and logits_BLE.dtype == torch.float32 and e <= 64 and (e & (e - 1)) == 0
+
+
 class Router(torch.nn.Module):
     def __init__(
         self,
@@ -148,6 +182,21 @@ class Router(torch.nn.Module):
     def forward(self, x_BLD: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         w_DE = _SumReplicatedGrads.apply(self.w_DE, self.sync_dim) if self.expert_parallel else self.w_DE
         logits_BLE = router_logits(x_BLD, w_DE)
+        if _route_kernel_usable(logits_BLE):
+            lead = logits_BLE.shape[:-1]
+            softmax = self.router == "softmax"
+            bias = None if softmax else self.expert_bias_E.to(torch.float32).contiguous()
+            weights_TK, indices_TK, probs_TE = _RouteTopK.apply(
+                logits_BLE.reshape(-1, self.n_experts).contiguous(), bias, 0 if softmax else 1, self.top_k,
+                float(self.route_scale))
+            weights_BLK = weights_TK.view(*lead, self.top_k)
+            indices_BLK = indices_TK.view(*lead, self.top_k)
+            if softmax:
+                probs_BLE = probs_TE.view(*lead, self.n_experts)
+                self.aux_loss = load_balancing_loss(probs_BLE, indices_BLK, self.aux_loss_coeff) if self.training else None
+            elif self.training:
+                self.update_bias(indices_BLK)
+            return weights_BLK, indices_BLK
         if self.router == "softmax":
             probs_BLE = torch.softmax(logits_BLE, dim=-1)
             indices_BLK = torch.topk(probs_BLE.detach(), self.top_k, dim=-1).indices

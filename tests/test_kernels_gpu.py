@@ -173,3 +173,37 @@ def test_router_logits_kernels_match_fp64(tokens, dim, experts):
     assert rel(x.grad, xd.grad) < 1e-5
     assert rel(w.grad, wd.grad) < 1e-5
     check_status()
+
+
+@pytest.mark.parametrize("mode", ["softmax", "sigmoid"])
+@pytest.mark.parametrize("experts,top_k", [(8, 2), (16, 4)])
+def test_routing_kernels_match_aten_router(mode, experts, top_k):
+    """Routing kernels (probabilities, top-k, weights and their backward)
+    against the same Router on CPU (ATen ops): indices equal, weights,
+    auxiliary loss and the x / w gradients close."""
+    import copy
+
+    from abacus_b200.models.moe import Router
+
+    torch.manual_seed(31)
+    cpu = Router(64, experts, top_k, router=mode, route_scale=2.5)
+    cpu.expert_bias_E.copy_(0.01 * torch.randn(experts))
+    gpu = copy.deepcopy(cpu).cuda()
+    x = torch.randn(3, 100, 64)
+    g = torch.randn(3, 100, top_k)
+    res = {}
+    for name, r, dev in (("cpu", cpu, "cpu"), ("gpu", gpu, "cuda")):
+        xi = x.to(dev).clone().requires_grad_()
+        w, idx = r(xi)
+        loss = (w * g.to(dev)).sum()
+        if r.aux_loss is not None:
+            loss = loss + 10 * r.aux_loss
+        loss.backward()
+        res[name] = (w.detach().cpu(), idx.cpu(), xi.grad.cpu(), r.w_DE.grad.cpu(), r.expert_bias_E.cpu())
+    wc, ic, gxc, gwc, bc = res["cpu"]
+    wg, ig, gxg, gwg, bg = res["gpu"]
+    assert torch.equal(ic, ig)
+    assert (wc - wg).abs().max().item() < 1e-5 * max(1.0, wc.abs().max().item())
+    assert (gxc - gxg).abs().max().item() < 1e-4 * gxc.abs().max().item()
+    assert (gwc - gwg).abs().max().item() < 1e-4 * gwc.abs().max().item()
+    assert torch.allclose(bc, bg)

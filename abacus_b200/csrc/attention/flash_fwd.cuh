@@ -68,7 +68,20 @@ struct FwdCfg {
   static constexpr int kStages = 2;
   static constexpr int kStageBytes = (kKBytes + kVBytes) * kSplit;
   static constexpr int kSmemRaw = kQBytes * kSplit + kStages * kStageBytes + 1024;
-  static constexpr int kThreads = PASSES == 3 ? 320 : 192;
+  // 3xTF32 at head_dim 64: each query row's softmax is shared by two warps
+  // (two warpgroups, 32 of the 64 key columns and 32 of the 64 output columns
+  // each), so a key block's exp / split / TMEM work is halved per thread; the
+  // row maxima and, at the end, the row sums are exchanged in shared memory.
+  // Warpgroups: 0 producer + MMA, 1 and 2 softmax halves, 3 converter, with a
+  // setmaxnreg split of 128 x (72 + 168 + 168 + 104) = 65536 registers.
+  static constexpr int kHalves = (PASSES == 3 && D == 64) ? 2 : 1;
+  static constexpr int kCtrlWarps = kHalves == 2 ? 4 : 2;
+  static constexpr int kSoftWarp0 = kCtrlWarps;
+  static constexpr int kConvWarp0 = kSoftWarp0 + 4 * kHalves;
+  static constexpr uint32_t kRegsCtrl = 72, kRegsSoft = 168, kRegsConv = 104;
+  static constexpr int kThreads = kHalves == 2 ? 512 : (PASSES == 3 ? 320 : 192);
+  static_assert(kHalves == 1 || 128 * (kRegsCtrl + 2 * kRegsSoft + kRegsConv) == kThreads * 128,
+                "warpgroup register budgets must add up to the launch's 65536");
   // Register cap for one CTA per SM: each of the 4 SM sub-partitions holds
   // 16384 registers and ceil(warps / 4) of the CTA's warps.
   static constexpr int kWarpsPerSubpartition = (kThreads / 32 + 3) / 4;
@@ -150,9 +163,9 @@ __global__ void __maxnreg__((FwdCfg<D, PASSES>::kMaxRegs)) flash_fwd_kernel(cons
       mbar_init(&v_conv[i], 128);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 128 * Cfg::kHalves);
       mbar_init(&pv_full[i], 1);
-      mbar_init(&pv_empty[i], 128);
+      mbar_init(&pv_empty[i], 128 * Cfg::kHalves);
     }
     fence_mbar_init();
   }
@@ -213,6 +226,8 @@ __global__ void __maxnreg__((FwdCfg<D, PASSES>::kMaxRegs)) flash_fwd_kernel(cons
   const int nb = n_blocks;
   if (threadIdx.x == 0) ABACUS_FWD_TRACE(8, 1)
 
+  if (warp < Cfg::kCtrlWarps) {
+  if constexpr (Cfg::kHalves == 2) regs_decrease<Cfg::kRegsCtrl>();
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (elect_one_sync()) {
@@ -334,7 +349,118 @@ __global__ void __maxnreg__((FwdCfg<D, PASSES>::kMaxRegs)) flash_fwd_kernel(cons
         }
       }
     }
-  } else if (warp < 6) {
+  }  // warps 2 and 3 of warpgroup 0 (split softmax) have no role
+  } else if (Cfg::kHalves == 2 && warp < Cfg::kConvWarp0) {
+    // ------------------------------------------------------- softmax, split
+    // Warp w of warpgroup 1 and warp w of warpgroup 2 hold the same 32 query
+    // rows (TMEM lanes); half h takes S / P columns [32 h, 32 h + 32) of each
+    // key block and output columns [32 h, 32 h + 32).
+    regs_increase<Cfg::kRegsSoft>();
+    __shared__ float xmax[2][2][kBlockM];  // [block parity][half][row]
+    __shared__ float xsum[2][kBlockM];
+    const int q = warp % 4;
+    const int half = (warp - Cfg::kSoftWarp0) / 4;
+    const int r = q * 32 + lane;
+    const int qi = m0 + r;
+    const int qpos = qi < p.lq ? (p.q_pos ? static_cast<int>(p.q_pos[qi]) : qi) : INT_MIN;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const bool tracer = threadIdx.x == Cfg::kSoftWarp0 * 32;
+    float o[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = 0.f;
+    float m = -FLT_MAX, l = 0.f, alpha_prev = 0.f;
+    // After a failed wait the warp keeps meeting its partner at every row
+    // exchange (a named barrier has no time limit) but skips the work.
+    bool dead = false;
+    for (int j = 0; j <= nb; ++j) {
+      float alpha = 1.f;
+      if (j < nb) {
+        const int s = j & 1;
+        const int entry = block_list[j];
+        const int kb = entry & 0xFFFF;
+        const bool partial = (entry >> 30) & 1;
+        if (!dead && !mbar_wait_warp(&s_full[s], (j >> 1) & 1, p.status, kStatusTimeoutAccum)) dead = true;
+        if (tracer) ABACUS_FWD_TRACE(4, j)
+        tc_fence_after();
+        float sv[32];
+        float bmax = -FLT_MAX;
+        if (!dead) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + s * Cfg::kSPCols + half * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(v[i]) * p.scale_log2;
+          if (partial) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int ki = kb * kBlockN + half * 32 + i;
+              const bool valid = ki < p.lk && (p.k_pos ? static_cast<int>(__ldg(p.k_pos + ki)) : ki) <= qpos;
+              if (!valid) sv[i] = -FLT_MAX;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) bmax = fmaxf(bmax, sv[i]);
+        }
+        xmax[j & 1][half][r] = bmax;
+        named_barrier_sync(1 + q, 64);
+        bmax = fmaxf(bmax, xmax[j & 1][half ^ 1][r]);
+        const float m_new = fmaxf(m, bmax);
+        alpha = (m == -FLT_MAX) ? 0.f : ex2_approx(m - m_new);
+        if (!dead) {
+          float bsum = 0.f;
+          uint32_t vh[32], vl[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float e = (sv[i] == -FLT_MAX) ? 0.f : ex2_approx(sv[i] - m_new);
+            bsum += e;
+            float hi, lo;
+            split_tf32(e, hi, lo);
+            vh[i] = __float_as_uint(hi);
+            vl[i] = __float_as_uint(lo);
+          }
+          tmem_st32(lane_base + s * Cfg::kSPCols + half * 32, vh);
+          tmem_st32(lane_base + s * Cfg::kSPCols + kBlockN + half * 32, vl);
+          l = l * alpha + bsum;
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(&p_full[s]);
+        }
+        m = m_new;
+        if (tracer) ABACUS_FWD_TRACE(5, j)
+      }
+      if (j >= 1 && !dead) {
+        // Fold this half of PV_{j-1}: o = o * alpha_{j-1} + PV_{j-1}.
+        const int s = (j - 1) & 1;
+        if (!mbar_wait_warp(&pv_full[s], ((j - 1) >> 1) & 1, p.status, kStatusTimeoutAccum)) {
+          dead = true;
+        } else {
+          if (tracer) ABACUS_FWD_TRACE(6, j - 1)
+          tc_fence_after();
+          uint32_t v[32];
+          tmem_ld32(lane_base + Cfg::kPVBase + s * D + half * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = o[i] * alpha_prev + __uint_as_float(v[i]);
+          tc_fence_before();
+          mbar_arrive(&pv_empty[s]);
+          if (tracer) ABACUS_FWD_TRACE(7, j - 1)
+        }
+      }
+      alpha_prev = alpha;
+    }
+    // The row sum is the two halves' sums.
+    xsum[half][r] = l;
+    named_barrier_sync(1 + q, 64);
+    l += xsum[half ^ 1][r];
+    if (!dead && qi < p.lq) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      float* orow = p.out + static_cast<long long>(q_row0 + r) * p.ld_o + col0 + half * 32;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(orow + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+      if (half == 0) p.lse[(static_cast<long long>(b) * p.heads + h) * p.lq + qi] = (m + log2f(l)) * 0.69314718055994531f;
+    }
+  } else if (warp < Cfg::kConvWarp0) {
     // ---------------------------------------------------------------- softmax
     const int q = warp % 4;
     const int r = q * 32 + lane;  // row within the block == TMEM lane
@@ -451,7 +577,8 @@ __global__ void __maxnreg__((FwdCfg<D, PASSES>::kMaxRegs)) flash_fwd_kernel(cons
     }
   } else if (PASSES == 3) {
     // ---------------------------------------------------------------- converter
-    const int ct = threadIdx.x - 192;
+    if constexpr (Cfg::kHalves == 2) regs_decrease<Cfg::kRegsConv>();
+    const int ct = threadIdx.x - Cfg::kConvWarp0 * 32;
     auto split = [&](uint8_t* hi_buf, uint8_t* lo_buf, int bytes) {
       float4* hi = reinterpret_cast<float4*>(hi_buf);
       float4* lo = reinterpret_cast<float4*>(lo_buf);

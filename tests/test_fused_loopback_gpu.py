@@ -13,8 +13,9 @@ Covered: the sequence-parallel all-gather fused into a waiting GEMM
 (``tp_push_rows`` + ``gemm_out_tp`` wait), the GEMM -> reduce-scatter
 epilogue with the owner-side reduction (``gemm_out_tp`` scatter +
 ``tp_reduce_rows``), the context-parallel flash forward over pushed K / V
-(``flash_attn_fwd_cp``), and the data-parallel reduce + AdamW + broadcast
-(``ar_adamw``).
+(``flash_attn_fwd_cp``), the data-parallel reduce + AdamW + broadcast
+(``ar_adamw``) and its ZeRO-3 local-slice form, and the expert-parallel
+dispatch / grouped experts / combine with static capacity slabs.
 """
 import math
 
@@ -216,3 +217,84 @@ def test_zero3_reduce_scatter_adamw_into_local_slices():
     v = (1 - b2) * g * g
     w = w - lr / (1 - b1) * m / ((v / (1 - b2)).sqrt() + eps)
     assert _rel(torch.cat(slices), w) < 1e-6
+
+
+def test_expert_parallel_dispatch_grouped_experts_combine():
+    """Expert parallelism with static capacity slabs: each emulated rank pushes
+    its assignments into the owning rank's expert slabs (ep_push_rows, over
+    capacity -> dropped), every rank runs its local experts as grouped
+    launches (the up-projection waits for all ranks' pushes, the
+    down-projection's epilogue returns rows to their source ranks by row map),
+    and each source combines its weighted rows (ep_credit for the dropped ones,
+    ep_combine). Oracle: the routed SwiGLU experts in fp64."""
+    precision.set_precision("fp32")
+    passes = precision.passes()
+    torch.manual_seed(5)
+    n, dim, hidden, top_k = 96, 128, 256, 2
+    local_experts = 2
+    n_experts = WORLD * local_experts
+    capacity = 40  # below the mean load of 48 per (source, expert): some rows drop
+    slab = WORLD * capacity
+    rows = local_experts * slab
+    xs = [torch.randn(n, dim, device="cuda") for _ in range(WORLD)]
+    idx = [torch.stack([torch.randperm(n_experts, device="cuda")[:top_k] for _ in range(n)]) for _ in range(WORLD)]
+    wts = [torch.rand(n, top_k, device="cuda") for _ in range(WORLD)]
+    wg = [torch.randn(local_experts, dim, hidden, device="cuda") / dim**0.5 for _ in range(WORLD)]
+    wu = [torch.randn(local_experts, dim, hidden, device="cuda") / dim**0.5 for _ in range(WORLD)]
+    wd = [torch.randn(local_experts, hidden, dim, device="cuda") / hidden**0.5 for _ in range(WORLD)]
+    slabs = [torch.zeros(rows, dim, device="cuda") for _ in range(WORLD)]
+    metas = [torch.full((rows,), -1, dtype=torch.int32, device="cuda") for _ in range(WORLD)]
+    sig = _signals()
+    off, epoch = 96, 1
+    rets = [torch.zeros(n * top_k, dim, device="cuda") for _ in range(WORLD)]
+    counters = [torch.zeros(1, dtype=torch.int32, device="cuda") for _ in range(WORLD)]
+    keeps, dropped = [], []
+    # Dispatch: every rank pushes before any expert GEMM runs.
+    for r in range(WORLD):
+        flat_e = idx[r].reshape(-1)
+        onehot = torch.nn.functional.one_hot(flat_e, n_experts)
+        within = (onehot.cumsum(dim=0) * onehot).sum(dim=-1) - 1
+        keep = within < capacity
+        dest_rank = torch.where(keep, flat_e // local_experts, -1).to(torch.int32)
+        dest_row = ((flat_e % local_experts) * slab + r * capacity + within.clamp(max=capacity - 1)).to(torch.int32)
+        done = torch.zeros(1, dtype=torch.int32, device="cuda")
+        flags = [_ptr(sig[p], off + r) for p in range(WORLD)]
+        ext().ep_push_rows(xs[r], top_k, dest_rank.contiguous(), dest_row.contiguous(), None,
+                           [s.data_ptr() for s in slabs], [m.data_ptr() for m in metas], flags, r, epoch, done)
+        keeps.append(keep.view(n, top_k))
+        dropped.append((~keep).sum().to(torch.int32).reshape(1))
+    # Experts: one grouped launch per product on each rank.
+    n_tiles = ext().gemm_n_tiles(dim, passes)
+    scatter_tail = [r_.data_ptr() for r_ in rets] + [c.data_ptr() for c in counters]
+    for p in range(WORLD):
+        x3 = slabs[p].view(local_experts, slab, dim)
+        g = torch.empty(local_experts, slab, hidden, device="cuda")
+        u = torch.empty_like(g)
+        h = torch.empty_like(g)
+        wait = [_ptr(sig[p], off), 2, epoch, 1, WORLD, p]
+        ext().gemm_swiglu_grouped(x3, wg[p], wu[p], g, u, h, passes, wait)
+        ext().gemm_grouped(rets[p].view(-1)[:dim].view(1, 1, dim), h, [wd[p]], False, False, SINGLE, 1.0, False, passes,
+                           [-1, metas[p].data_ptr()] + scatter_tail)
+    # Combine on every source.
+    outs = []
+    for r in range(WORLD):
+        ext().ep_credit(counters[r], dropped[r], n_tiles)
+        out = torch.empty(n, dim, device="cuda")
+        w_kept = (wts[r] * keeps[r]).contiguous()
+        ext().ep_combine(rets[r], w_kept, top_k, counters[r], n * top_k * n_tiles, out)
+        outs.append(out)
+    torch.cuda.synchronize()
+    check_status()
+    for r in range(WORLD):
+        want = torch.zeros(n, dim, dtype=torch.float64, device="cuda")
+        xd = xs[r].double()
+        for t in range(n):
+            for j in range(top_k):
+                if not keeps[r][t, j]:
+                    continue
+                e = int(idx[r][t, j])
+                o, le = divmod(e, local_experts)
+                hdn = torch.nn.functional.silu(xd[t] @ wg[o][le].double()) * (xd[t] @ wu[o][le].double())
+                want[t] += wts[r][t, j].double() * (hdn @ wd[o][le].double())
+        assert _rel(outs[r], want) < 1e-5
+    assert sum(int(d) for d in dropped) > 0  # the capacity limit was exercised

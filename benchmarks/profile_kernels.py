@@ -11,8 +11,9 @@ on a one-rank group: the peer tables hold this GPU only, so the figures are
 the kernels' own memory-side cost (NVLink is exercised by the multi-GPU tests
 and benchmarks).
 
-Each family runs twice (warm-up + profiled launch) and prints its device time
-(CUDA events) of the second run.
+Each family runs three warm-up calls and then ten timed calls back to back,
+and prints the mean device time of one call (CUDA events); a profiler with
+`-s 1 -c 1` captures the second (warm-up) launch.
 """
 import math
 import os
@@ -31,15 +32,22 @@ from abacus_b200.ops.norm import rmsnorm  # noqa: E402
 from abacus_b200.optim.adamw import AdamW  # noqa: E402
 
 
-def timed(fn):
-    fn()
+def timed(fn, reps=10):
+    """Mean device time of one call over `reps` back-to-back calls after three
+    warm-up calls (CUDA events on the launching stream, synchronised on both
+    sides). Back to back, the host-side launch cost of one call overlaps the
+    previous call's kernels instead of being timed; inputs that fit in L2 stay
+    there between calls."""
+    for _ in range(3):
+        fn()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    fn()
+    for _ in range(reps):
+        fn()
     b.record()
     torch.cuda.synchronize()
-    return a.elapsed_time(b)
+    return a.elapsed_time(b) / reps
 
 
 def run(name):

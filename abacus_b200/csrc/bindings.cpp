@@ -26,6 +26,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router_logits_bwd", &abacus::ops::router_logits_bwd, "gradients of the router scores");
   m.def("route_topk", &abacus::ops::route_topk, "MoE routing: probabilities, top-k experts and weights (E <= 64)");
   m.def("route_topk_bwd", &abacus::ops::route_topk_bwd, "gradient of the routing logits");
+  m.def("expert_rank", &abacus::ops::expert_rank, "per-expert rank of each assignment (capacity slots)");
   m.def("transpose2d", &abacus::ops::transpose2d, "out = in^T (fp32, tiled)");
   m.def("rmsnorm_fwd", &abacus::ops::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &abacus::ops::rmsnorm_bwd);

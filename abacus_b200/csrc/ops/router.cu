@@ -248,6 +248,38 @@ __global__ void __launch_bounds__(256) route_topk_bwd_kernel(const float* __rest
   }
 }
 
+// Rank of every assignment among the assignments to the same expert, in
+// assignment order (the capacity slot of static expert slabs): one block per
+// expert walks the assignments in chunks of blockDim, a block-wide exclusive
+// scan of the match flags giving each match its rank. Deterministic.
+__global__ void __launch_bounds__(1024) expert_rank_kernel(const int64_t* __restrict__ experts, long long n,
+                                                           int64_t* __restrict__ rank) {
+  __shared__ int warp_sums[32];
+  __shared__ long long carry;
+  const int e = blockIdx.x;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, warps = blockDim.x / 32;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (long long base = 0; base < n; base += blockDim.x) {
+    const long long a = base + threadIdx.x;
+    const int hit = (a < n && experts[a] == e) ? 1 : 0;
+    const unsigned ballot = __ballot_sync(0xffffffffu, hit);
+    const int before_in_warp = __popc(ballot & ((1u << lane) - 1u));
+    if (lane == 0) warp_sums[warp] = __popc(ballot);
+    __syncthreads();
+    int before_warps = 0, total = 0;
+    for (int w = 0; w < warps; ++w) {
+      const int c = warp_sums[w];
+      before_warps += w < warp ? c : 0;
+      total += c;
+    }
+    if (hit) rank[a] = carry + before_warps + before_in_warp;
+    __syncthreads();
+    if (threadIdx.x == 0) carry += total;
+    __syncthreads();
+  }
+}
+
 }  // namespace
 
 void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor logits) {
@@ -373,6 +405,27 @@ void route_topk_bwd(torch::Tensor probs, torch::Tensor indices, torch::Tensor dw
                                                    static_cast<int>(top_k), static_cast<float>(route_scale), tokens,
                                                    dlogits.data_ptr<float>());
   })
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  abacus::host::note_launch();
+}
+
+}  // namespace ops
+}  // namespace abacus
+
+namespace abacus {
+namespace ops {
+
+void expert_rank(torch::Tensor experts, int64_t n_experts, torch::Tensor rank) {
+  const c10::cuda::CUDAGuard guard(experts.device());
+  TORCH_CHECK(experts.is_cuda() && experts.scalar_type() == torch::kInt64 && experts.is_contiguous(),
+              "experts: contiguous int64 assignment list");
+  TORCH_CHECK(rank.is_cuda() && rank.scalar_type() == torch::kInt64 && rank.is_contiguous() &&
+                  rank.numel() == experts.numel(),
+              "rank: int64, one per assignment");
+  TORCH_CHECK(n_experts >= 1 && n_experts <= 65535, "1..65535 experts");
+  if (experts.numel() == 0) return;
+  expert_rank_kernel<<<static_cast<unsigned>(n_experts), 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+      experts.data_ptr<int64_t>(), experts.numel(), rank.data_ptr<int64_t>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   abacus::host::note_launch();
 }

@@ -15,5 +15,8 @@ void route_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_t
 void route_topk_bwd(torch::Tensor probs, torch::Tensor indices, torch::Tensor dweights,
                     c10::optional<torch::Tensor> dprobs, int64_t mode, int64_t top_k, double route_scale,
                     torch::Tensor dlogits);
+// rank[a] = number of earlier assignments (in list order) to the same expert
+// as assignment a: the capacity slot of static expert slabs.
+void expert_rank(torch::Tensor experts, int64_t n_experts, torch::Tensor rank);
 }  // namespace ops
 }  // namespace abacus

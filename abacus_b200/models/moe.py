@@ -42,6 +42,7 @@ import torch
 
 from abacus_b200.ops import gemm
 from abacus_b200.ops._ext import ext
+from abacus_b200.ops.routing import expert_rank
 from abacus_b200.parallel import ep_fused, mesh, tp_fused
 from abacus_b200.parallel.expert_parallel import (
     _AllToAll,
@@ -229,9 +230,7 @@ class Router(torch.nn.Module):
 def _capacity_keep(indices_TK: torch.Tensor, n_experts: int, capacity: int) -> torch.Tensor:
     """Mask (T, K) of kept assignments: the first `capacity` per expert in
     (token, slot) order."""
-    flat = indices_TK.reshape(-1)
-    onehot = torch.nn.functional.one_hot(flat, n_experts)
-    rank_in_expert = (onehot.cumsum(dim=0) * onehot).sum(dim=-1) - 1
+    rank_in_expert = expert_rank(indices_TK.reshape(-1), n_experts)
     return (rank_in_expert < capacity).reshape(indices_TK.shape)
 
 
@@ -269,8 +268,7 @@ def _grouped_experts_capacity(x_TD, weights_TK, indices_TK, w_gate_EDM, w_up_EDM
     t, k = indices_TK.shape
     n_experts = w_gate_EDM.shape[0]
     flat_e = indices_TK.reshape(-1)
-    onehot = torch.nn.functional.one_hot(flat_e, n_experts)
-    within = (onehot.cumsum(dim=0) * onehot).sum(dim=-1) - 1
+    within = expert_rank(flat_e, n_experts)
     keep = within < capacity
     spill = n_experts * capacity
     slot = torch.where(keep, flat_e * capacity + within, spill)

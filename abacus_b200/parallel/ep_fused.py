@@ -45,6 +45,7 @@ import torch.distributed as dist
 
 from abacus_b200.ops import precision
 from abacus_b200.ops._ext import ext
+from abacus_b200.ops.routing import expert_rank
 from abacus_b200.parallel import mesh, tp_fused
 
 DIM = "ep"
@@ -214,8 +215,7 @@ def _static_plan(indices, n_experts, local_experts, capacity, ws):
     (dest_rank, dest_row) int32 (dest_rank -1 = dropped), the keep mask and
     the number of dropped assignments (int32, on the device)."""
     flat_e = indices.reshape(-1)
-    onehot = torch.nn.functional.one_hot(flat_e, n_experts)
-    within = (onehot.cumsum(dim=0) * onehot).sum(dim=-1) - 1  # rank among this expert's assignments
+    within = expert_rank(flat_e, n_experts)  # rank among this expert's assignments
     keep = within < capacity
     slab = ws.world * capacity
     dest_rank = torch.where(keep, torch.div(flat_e, local_experts, rounding_mode="floor"), -1).to(torch.int32)

@@ -207,3 +207,15 @@ def test_routing_kernels_match_aten_router(mode, experts, top_k):
     assert (gxc - gxg).abs().max().item() < 1e-4 * gxc.abs().max().item()
     assert (gwc - gwg).abs().max().item() < 1e-4 * gwc.abs().max().item()
     assert torch.allclose(bc, bg)
+
+
+@pytest.mark.parametrize("n,experts", [(100003, 8), (4097, 64), (5, 3)])
+def test_expert_rank_kernel_matches_prefix_count(n, experts):
+    """Capacity-slot ranks from the scan kernel against the CPU one-hot prefix sum."""
+    from abacus_b200.ops.routing import expert_rank
+
+    torch.manual_seed(41)
+    flat = torch.randint(0, experts, (n,))
+    got = expert_rank(flat.cuda(), experts).cpu()
+    want = expert_rank(flat, experts)
+    assert torch.equal(got, want)

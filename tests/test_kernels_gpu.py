@@ -219,3 +219,19 @@ def test_expert_rank_kernel_matches_prefix_count(n, experts):
     got = expert_rank(flat.cuda(), experts).cpu()
     want = expert_rank(flat, experts)
     assert torch.equal(got, want)
+
+
+def test_static_expert_parallel_plan_on_device():
+    """The fused EP path's slab placement (ranks from the scan kernel) against
+    the same plan computed on CPU."""
+    from types import SimpleNamespace
+
+    from abacus_b200.parallel import ep_fused
+
+    torch.manual_seed(43)
+    idx = torch.randint(0, 8, (500, 2))
+    ws = SimpleNamespace(world=2, rank=1)
+    got = ep_fused._static_plan(idx.cuda(), 8, 4, 100, ws)
+    want = ep_fused._static_plan(idx, 8, 4, 100, ws)
+    for g, w in zip(got, want):
+        assert torch.equal(g.cpu(), w)
